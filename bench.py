@@ -1,0 +1,343 @@
+#!/usr/bin/env python
+"""Benchmark of the quantized-weight decode path: Q4_K GEMV weight GB/s.
+
+Workload: W = 11008 x 4096 in GGUF Q4_K (25,362,432 bytes of blocks), one bf16
+activation row (M = 1), fp32 output -- the decode point of the Q4_K
+dequant-GEMM sweep.  One step = one call of the fused dequant-GEMV (activation
+split + GEMV, two launches) on one weight matrix.  Steps rotate over 16
+distinct weight copies (406 MB, more than 3x the 126 MB L2), so every step
+streams its weight from HBM.  Weights and activations are seeded synthetic
+data (random-init blocks with the documented value distributions).
+
+Printed line (rank 0): ``value`` = quantized weight bytes of all steps of all
+ranks / max-over-ranks device time of the timed graph replay; ``e2e`` = the
+same metric through the public ``LinearOp.forward`` with the activation coming
+from pinned host memory and the result read back every step; ``roofline`` =
+the GEMV kernel alone against the measured HBM copy bandwidth;
+``cpu_baseline`` = the numpy restatement of the reference's path (fp32 x @ W.T
+on the dequantized weight) on this host's cores.
+
+``--impl reference`` times the reference's CPU path (the numpy port in
+``oracle/``) on the same workload instead.  Multi-GPU (torchrun): every rank
+runs the same per-GPU workload on its own weights (weak scaling; the row
+blocks are independent, so there is no collective in the data path).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+QTYPE, N, K, M = "Q4_K", 11008, 4096, 1
+W_BYTES = N * (K // 256) * 144          # 25,362,432
+COPIES = 16
+METRIC = "Q4_K GEMV weight GB/s"
+UNIT = "GB/s"
+# DRAM bytes read+written per launch of the GEMV kernel (k_qgemv_q4k_dp4a<1>),
+# from ncu on the same kernel and shape; None until a capture exists.
+NCU_TRAFFIC_PER_LAUNCH = None
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def config(extra=None):
+    c = {"workload": f"{QTYPE} GEMV {N}x{K}, M={M}, bf16 activations, fp32 out",
+         "weight_bytes": W_BYTES, "weight_copies": COPIES,
+         "l2_policy": f"inputs larger than L2: {COPIES} rotating weight copies = {COPIES * W_BYTES / 1e6:.0f} MB",
+         "parallelism": "independent replicas per GPU (row blocks), no collective"}
+    if extra:
+        c.update(extra)
+    return c
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        self.idx = ids[gpu_index] if gpu_index < len(ids) and ids[gpu_index].isdigit() else gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.15)
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        rows = [r.split(",") for r in self.out.strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's per-step work (fp32 x @ W.T on the weight it
+# dequantized at load), restated in numpy in oracle/
+# ---------------------------------------------------------------------------
+def cpu_port_setup(raw, x_bf16_as_f32):
+    from oracle import gguf_dequant_oracle as O
+    w32 = O.dequantize(raw, QTYPE, (N, K)).astype(np.float32)
+    return w32, x_bf16_as_f32.reshape(M, K)
+
+
+def blas_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads") for i in threadpool_info() if i.get("user_api") == "blas"]
+        return int(n[0]) if n else os.cpu_count()
+    except Exception:  # noqa: BLE001
+        return os.cpu_count()
+
+
+def time_cpu_port(w32, x, budget_s=10.0, max_iters=5000, min_iters=20):
+    from oracle.moe_oracle import linear
+    linear(x, w32)  # warm
+    t0 = time.perf_counter()
+    it = 0
+    while it < max_iters and (it < min_iters or time.perf_counter() - t0 < budget_s):
+        linear(x, w32)
+        it += 1
+    dt = (time.perf_counter() - t0) / it
+    return dt, it
+
+
+# ---------------------------------------------------------------------------
+def dist_setup(backend):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        import datetime
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    return rank, world, local
+
+
+def run_reference(args):
+    rank, world, local = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), 0
+    if rank != 0:
+        return
+    from xanosmerks_b200.synth import make_weight
+    raw = make_weight(QTYPE, N, K, seed=0)
+    xb = (np.random.default_rng(1).standard_normal((M, K)).astype(np.float32).view(np.uint32) >> 16 << 16).view(np.float32)
+    w32, x = cpu_port_setup(raw, xb)
+    from oracle.moe_oracle import linear
+    for _ in range(args.warmup):
+        linear(x, w32)
+    ts = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        linear(x, w32)
+        ts.append(time.perf_counter() - t0)
+    dt = sum(ts) / len(ts)
+    v = W_BYTES / dt / 1e9
+    cores = blas_threads()
+    out = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": UNIT, "n_gpus": args.gpus,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": config({"reference_path": "numpy port of LinearOp.forward (ops.py:62-67) on the weight "
+                                               "dequantized at load (gguf_dequant.py:309-341), host CPU"}),
+           "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": cores, "kind": "port",
+                            "sample": f"{args.steps} steps of fp32 (1x{K}) @ ({K}x{N}) numpy/BLAS"},
+           "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    rank, world, local = dist_setup("nccl")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from xanosmerks_b200 import _lib
+    from xanosmerks_b200.ops import GGUFTensor, LinearOp
+    from xanosmerks_b200.synth import make_weight
+    lib = _lib.lib
+    qid = 12
+
+    raw = make_weight(QTYPE, N, K, seed=rank)
+    w0 = torch.from_numpy(raw).to(dev)
+    ws = [w0] + [w0.clone() for _ in range(COPIES - 1)]
+    xb = (np.random.default_rng(1).standard_normal((M, K)).astype(np.float32).view(np.uint32) >> 16 << 16).view(np.float32)
+    x_dev = torch.from_numpy(xb).to(dev).to(torch.bfloat16)
+    wsz = lib.xm_qgemv_workspace_size(K, M)
+    work = torch.empty(wsz, dtype=torch.uint8, device=dev)
+    y = torch.empty((M, N), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    # launches go to torch's current stream, which is the capture stream inside torch.cuda.graph
+    def step(i):
+        w = ws[i % COPIES]
+        _lib.check(lib.xm_qgemv(qid, w.data_ptr(), W_BYTES, N, K, x_dev.data_ptr(), _lib.DT_BF16, M, None,
+                                y.data_ptr(), work.data_ptr(), wsz, torch.cuda.current_stream().cuda_stream), "qgemv")
+
+    def gemv_only(i):
+        w = ws[i % COPIES]
+        _lib.check(lib.xm_qgemv_presplit(qid, w.data_ptr(), W_BYTES, N, K, M, work.data_ptr(), wsz, None,
+                                         y.data_ptr(), torch.cuda.current_stream().cuda_stream), "qgemv_presplit")
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize()
+
+    def capture(fn, count):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(count):
+                fn(i)
+        return g
+
+    g_steps = capture(step, args.steps)
+    g_gemv = capture(gemv_only, args.steps)
+    for _ in range(2):
+        g_steps.replay()
+        g_gemv.replay()
+    torch.cuda.synchronize()
+
+    def timed(graph):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+            dist.barrier()
+        return ms
+
+    with Clocks(local) as clk:
+        ms_steps = timed(g_steps)
+        ms_gemv = timed(g_gemv)
+    clocks = clk.summary()
+
+    # correctness guard on the last result (rank-local, cheap): exact path on the same weight
+    y_exact = torch.empty_like(y)
+    w_last = ws[(args.steps - 1) % COPIES]
+    _lib.check(lib.xm_qgemv_exact(qid, w_last.data_ptr(), W_BYTES, N, K, x_dev.data_ptr(), _lib.DT_BF16, M, None,
+                                  y_exact.data_ptr(), stream.cuda_stream), "qgemv_exact")
+    g_steps.replay()
+    torch.cuda.synchronize()
+    err = float((y - y_exact).abs().max() / y_exact.abs().max())
+
+    # end to end through the public API: pinned host activation in, fp32 result back to host, every step
+    ops = [LinearOp(GGUFTensor(w, QTYPE, (N, K))) for w in ws]
+    x_pin = torch.from_numpy(xb).to(torch.bfloat16).pin_memory()
+    e2e_steps = min(args.steps, 200)
+    for i in range(5):
+        ops[i % COPIES].forward(x_pin)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        out = ops[i % COPIES].forward(x_pin)
+    t_e2e = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([t_e2e], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_e2e = float(t.item())
+    assert out.shape == (M, N)
+    e2e = {"value": round(world * e2e_steps * W_BYTES / t_e2e / 1e9, 3), "unit": UNIT,
+           "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 4,
+           "api": "xanosmerks_b200.ops.LinearOp(GGUFTensor).forward(pinned bf16 host tensor)",
+           "ms_per_step": round(t_e2e / e2e_steps * 1e3, 4)}
+
+    value = world * args.steps * W_BYTES / (ms_steps / 1e3) / 1e9
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    G = K // 32
+    alg_bytes = W_BYTES + M * G * 80 + M * N * 4       # blocks + activation split + y
+    avg_gemv_s = ms_gemv / 1e3 / args.steps
+    achieved = alg_bytes / avg_gemv_s / 1e9
+    roofline = {"bound": "hbm", "kernel": "k_qgemv_q4k_dp4a<1>", "achieved": round(achieved, 1),
+                "peak": peak, "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "traffic": NCU_TRAFFIC_PER_LAUNCH, "algorithmic_bytes_per_launch": alg_bytes,
+                "avg_launch_us": round(avg_gemv_s * 1e6, 3)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        w32, xc = cpu_port_setup(raw, xb)
+        dt, it = time_cpu_port(w32, xc)
+        cpu = {"value": round(W_BYTES / dt / 1e9, 3), "unit": UNIT, "cores": blas_threads(), "kind": "port",
+               "sample": f"{it} steps of fp32 (1x{K}) @ ({K}x{N}) numpy/BLAS on the dequantized weight (~10 s)"}
+
+    if rank == 0:
+        out = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+               "warmup": args.warmup, "ms_per_step": round(ms_steps / args.steps, 6), "higher_is_better": True,
+               "scaling": "weak", "vs_baseline": None, "dtype": "i32 dp4a + f32", "data": "synthetic",
+               "config": config({"max_rel_err_vs_exact_path": err}), "e2e": e2e, "roofline": roofline,
+               "cpu_baseline": cpu, "clocks": clocks, "gpu_launches": 2 * args.steps}
+        print(json.dumps(out), flush=True)
+    del g_steps, g_gemv
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,111 @@
+/*
+ * xm_gguf.h -- C ABI of the B200 (sm_100a) GGUF quantized-weight path.
+ *
+ * Every entry point takes plain device pointers, byte/element counts and a
+ * CUDA stream (a cudaStream_t passed as void*, NULL = legacy default stream).
+ * Nothing here allocates device memory unless stated; buffers belong to the
+ * caller.  Calls are asynchronous on `stream`; argument errors are detected on
+ * the host before any launch.
+ *
+ * Return value: XM_OK (0) or a negative XM_ERR_* status; xm_last_error()
+ * gives the message of the last failure on the calling thread.
+ *
+ * Type ids (`qtype`) are the GGML numbers of the reference's GGUF reader
+ * (dtype_map.py:33-65): F32=0 F16=1 Q4_0=2 Q4_1=3 Q5_0=6 Q5_1=7 Q8_0=8
+ * Q8_1=9 Q2_K=10 Q3_K=11 Q4_K=12 Q5_K=13 Q6_K=14 Q8_K=15 I8=24 I16=25
+ * I32=26 I64=27 BF16=30.  IQ and TQ types are rejected with
+ * XM_ERR_UNSUPPORTED, as the reference raises NotImplementedError for them
+ * (gguf_dequant.py:493-501).
+ *
+ * Weight layout: a 2-D weight W[n][k] is the GGUF byte stream of n rows, each
+ * row k/QK consecutive block records (GGUF dims = [k, n]).  This is the byte
+ * order the reference dequantizes (gguf_dequant.py:31-32, loaders.py:340-343).
+ */
+#ifndef XM_GGUF_H
+#define XM_GGUF_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define XM_OK 0
+#define XM_ERR_INVALID (-1)     /* bad size / shape / pointer / alignment (numpy ValueError in the reference) */
+#define XM_ERR_UNSUPPORTED (-2) /* type not implemented (NotImplementedError in the reference) */
+#define XM_ERR_CUDA (-3)        /* CUDA runtime error */
+
+/* element types of activations and outputs */
+#define XM_DT_F32 0
+#define XM_DT_F16 1
+#define XM_DT_BF16 2
+
+/* ABI version of this header (bumped on any signature change). */
+int xm_abi_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* xm_last_error(void);
+
+/* Block geometry of a type: elements per block and bytes per block record.
+ * Replaces the lookup in GGUF_TYPE_BLOCK_SIZE (dtype_map.py:68-79). */
+int xm_qtype_info(int qtype, int* qk, int* record_bytes);
+
+/*
+ * Dequantize `n_elements` values of GGUF type `qtype` from the raw block bytes
+ * at `d_raw` (`raw_bytes` long; extra bytes are ignored) into `d_out`
+ * (XM_DT_F16: the reference's fp16 result, bit for bit; XM_DT_F32: the fp32
+ * value the reference holds before its final fp16 cast).  `d_out` must be
+ * 16-byte aligned.
+ *
+ * Replaces gguf_dequant.py:477-523 `dequantize(raw_bytes, tensor_type, shape)`
+ * and the per-type `dequant_<q>(raw_bytes, shape)` of gguf_dequant.py:25-455
+ * (and meanflare convert.py:46 `dequantize_gguf_tensor`).  The shape only
+ * fixes n_elements = prod(shape); the element order is the flat GGUF order.
+ */
+int xm_dequantize(int qtype, const void* d_raw, int64_t raw_bytes, int64_t n_elements,
+                  void* d_out, int out_dtype, void* stream);
+
+/*
+ * Decode GEMV: y[m][n] = sum_k x[m][k] * W[n][k] (+ bias[n]) for 1 <= m <= 8,
+ * W the GGUF blocks at `d_w` (`w_bytes` long, n rows of k elements), x
+ * row-major [m][k] of x_dtype (16-byte aligned), y row-major [m][n] fp32,
+ * bias fp32 [n] or NULL.  Fused: the blocks are unpacked in registers and
+ * never written back.
+ *
+ * `d_workspace` (16-byte aligned, >= xm_qgemv_workspace_size(k, m) bytes)
+ * holds the activation split of the integer-dot path; with NULL the call takes
+ * the exact path (each weight rounded to the reference's fp16 value).  Results
+ * of both paths are within 1e-3 of the reference (max abs error / max |y|).
+ *
+ * Replaces the decode-time `x @ W.T` on dequantized weights: ops.py:62-67
+ * `LinearOp.forward`, forward.py:93-101 (MLP), attention.py:47-51/:135
+ * (projections), forward.py:158 (lm_head), all after gguf_dequant.dequantize.
+ */
+int64_t xm_qgemv_workspace_size(int64_t k, int64_t m);
+int xm_qgemv(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k,
+             const void* d_x, int x_dtype, int64_t m, const float* d_bias, float* d_y,
+             void* d_workspace, int64_t workspace_bytes, void* stream);
+
+/*
+ * The two halves of the integer-dot GEMV, for callers that feed one activation
+ * to several weights (Q/K/V, gate/up): xm_split_activation writes the split of
+ * x into the workspace once; xm_qgemv_presplit runs the GEMV from it.  Types
+ * without an integer-dot path return XM_ERR_UNSUPPORTED from the latter.
+ */
+int xm_split_activation(const void* d_x, int x_dtype, int64_t m, int64_t k,
+                        void* d_workspace, int64_t workspace_bytes, void* stream);
+int xm_qgemv_presplit(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k,
+                      int64_t m, const void* d_workspace, int64_t workspace_bytes,
+                      const float* d_bias, float* d_y, void* stream);
+
+/* The exact path of xm_qgemv alone (every weight rounded to the reference's
+ * fp16 value, fp32 products); the cross-check of the integer-dot path. */
+int xm_qgemv_exact(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k,
+                   const void* d_x, int x_dtype, int64_t m, const float* d_bias, float* d_y,
+                   void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* XM_GGUF_H */

@@ -1,0 +1,71 @@
+"""ctypes binding of ``libxm_gguf.so`` (the C ABI declared in ``include/xm_gguf.h``).
+
+The library is required: there is no CPU fallback.  Importing this module
+fails with ``ImportError`` when the shared library has not been built
+(``python -m xanosmerks_b200.build``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libxm_gguf.so")
+
+XM_OK = 0
+XM_ERR_INVALID = -1
+XM_ERR_UNSUPPORTED = -2
+XM_ERR_CUDA = -3
+
+DT_F32, DT_F16, DT_BF16 = 0, 1, 2
+
+_i64 = ctypes.c_int64
+_vp = ctypes.c_void_p
+_int = ctypes.c_int
+
+# name -> (restype, argtypes); every symbol the header declares
+SIGNATURES = {
+    "xm_abi_version": (_int, []),
+    "xm_last_error": (ctypes.c_char_p, []),
+    "xm_qtype_info": (_int, [_int, ctypes.POINTER(_int), ctypes.POINTER(_int)]),
+    "xm_dequantize": (_int, [_int, _vp, _i64, _i64, _vp, _int, _vp]),
+    "xm_qgemv_workspace_size": (_i64, [_i64, _i64]),
+    "xm_qgemv": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _int, _i64, _vp, _vp, _vp, _i64, _vp]),
+    "xm_qgemv_exact": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _int, _i64, _vp, _vp, _vp]),
+    "xm_split_activation": (_int, [_vp, _int, _i64, _i64, _vp, _i64, _vp]),
+    "xm_qgemv_presplit": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp]),
+}
+
+
+class XMError(RuntimeError):
+    """A CUDA-side failure reported by the library."""
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing: build the CUDA library with `python -m xanosmerks_b200.build` "
+            f"(there is no CPU fallback)")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+
+
+def check(status: int, what: str = "") -> None:
+    """Map an XM_* status to the exception the reference raises for the same condition."""
+    if status == XM_OK:
+        return
+    msg = lib.xm_last_error().decode(errors="replace")
+    if what:
+        msg = f"{what}: {msg}"
+    if status == XM_ERR_UNSUPPORTED:
+        raise NotImplementedError(msg)
+    if status == XM_ERR_INVALID:
+        raise ValueError(msg)
+    raise XMError(msg)
