@@ -46,6 +46,11 @@ int xm_abi_version(void);
 /* Message of the last failing call on this thread ("" if none). */
 const char* xm_last_error(void);
 
+/* Device error word of the current device: a non-zero bit means a bounded wait
+ * inside a kernel gave up (XM_DEVERR_TIMEOUT = 1) instead of hanging.  With
+ * clear != 0 the word is reset.  Returns the word (>= 0) or XM_ERR_CUDA. */
+int xm_device_status(int clear);
+
 /* Block geometry of a type: elements per block and bytes per block record.
  * Replaces the lookup in GGUF_TYPE_BLOCK_SIZE (dtype_map.py:68-79). */
 int xm_qtype_info(int qtype, int* qk, int* record_bytes);
