@@ -109,6 +109,20 @@ int xm_qgemv_exact(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64
                    const void* d_x, int x_dtype, int64_t m, const float* d_bias, float* d_y,
                    void* stream);
 
+/*
+ * xm_qgemv without a workspace argument, for callers that cannot allocate
+ * device memory (a host runtime that owns the allocator, a process that must
+ * not allocate after start-up).  The activation split lives in a fixed array
+ * built into this library, 320 KiB per GPU (limit: m <= 8 with k <= 16384;
+ * larger requests return XM_ERR_INVALID).  The first call on each device
+ * looks up that array's address (cudaGetSymbolAddress), so make it before any
+ * stream capture.  Calls share the array: calls that overlap on the GPU race.
+ * Nothing is allocated.  This entry point has no counterpart in the reference.
+ */
+int xm_qgemv_noalloc(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k,
+                     const void* d_x, int x_dtype, int64_t m, const float* d_bias, float* d_y,
+                     void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -28,12 +28,14 @@ SIGNATURES = {
     "xm_abi_version": (_int, []),
     "xm_last_error": (ctypes.c_char_p, []),
     "xm_qtype_info": (_int, [_int, ctypes.POINTER(_int), ctypes.POINTER(_int)]),
+    "xm_device_status": (_int, [_int]),
     "xm_dequantize": (_int, [_int, _vp, _i64, _i64, _vp, _int, _vp]),
     "xm_qgemv_workspace_size": (_i64, [_i64, _i64]),
     "xm_qgemv": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _int, _i64, _vp, _vp, _vp, _i64, _vp]),
     "xm_qgemv_exact": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _int, _i64, _vp, _vp, _vp]),
     "xm_split_activation": (_int, [_vp, _int, _i64, _i64, _vp, _i64, _vp]),
     "xm_qgemv_presplit": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp]),
+    "xm_qgemv_noalloc": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _int, _i64, _vp, _vp, _vp]),
 }
 
 

@@ -16,6 +16,7 @@
 //   take): each weight is decoded to the reference's fp16 value and multiplied
 //   in fp32.  Slower; it is the fallback and the cross-check.
 #include <algorithm>
+#include <mutex>
 
 #include "xm_qtypes.cuh"
 
@@ -892,4 +893,68 @@ extern "C" int xm_qgemv(int qtype, const void* d_w, int64_t w_bytes, int64_t n, 
 extern "C" int xm_qgemv_exact(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k, const void* d_x,
                               int x_dtype, int64_t m, const float* d_bias, float* d_y, void* stream) {
   return xm_qgemv(qtype, d_w, w_bytes, n, k, d_x, x_dtype, m, d_bias, d_y, nullptr, 0, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free GEMV.
+//
+// Some callers cannot allocate device memory at all: code running under a
+// runtime that owns the device allocator (a host program that hands this
+// library only the tensors it already has), an environment that forbids
+// cudaMalloc after start-up, or a plugin that must not grow the process's
+// device footprint per call.  For them, xm_qgemv_noalloc keeps the
+// activation split (the only scratch the decode GEMV needs) in a fixed
+// array compiled into this library instead of a caller-supplied workspace.
+//
+// The array is a file-scope __device__ variable, so every GPU that loads the
+// library holds its own copy, kNoAllocScratchBytes long, until the process
+// exits.  Its host-side name is only a stand-in for the device address, so the
+// address is fetched with cudaGetSymbolAddress once per device (with that
+// device current), on the first call made on that device; that first call
+// should therefore happen before any stream capture.  Calls share the array:
+// two calls whose kernels overlap on the GPU (different streams, no ordering
+// between them) race on it.  Every call rewrites all of the split it later
+// reads, so nothing in the array has to start at zero.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int64_t kNoAllocScratchBytes = 8 * (16384 / 32) * (kPieceBytes + 16);   // m <= 8, k <= 16384: 320 KiB
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+struct NoAllocTable {
+  std::mutex mu;
+  void* ptr[64] = {};
+};
+NoAllocTable& noalloc_table() {
+  static NoAllocTable t;
+  return t;
+}
+}  // namespace
+
+extern "C" int xm_qgemv_noalloc(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k,
+                                const void* d_x, int x_dtype, int64_t m, const float* d_bias, float* d_y,
+                                void* stream) {
+  const int64_t need = xm_qgemv_workspace_size(k, m);
+  if (need > kNoAllocScratchBytes)
+    return xm_set_error(XM_ERR_INVALID,
+                        "qgemv_noalloc: m=%lld, k=%lld needs %lld bytes of split scratch; the built-in array holds "
+                        "%lld (m <= 8 with k <= 16384)",
+                        (long long)m, (long long)k, (long long)need, (long long)kNoAllocScratchBytes);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemv_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return xm_set_error(XM_ERR_INVALID, "qgemv_noalloc: device id %d out of range", dev);
+  void* scratch = nullptr;
+  {
+    NoAllocTable& t = noalloc_table();
+    std::lock_guard<std::mutex> lock(t.mu);
+    if (!t.ptr[dev]) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+      if (e != cudaSuccess || !p)
+        return xm_set_error(XM_ERR_CUDA, "qgemv_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      t.ptr[dev] = p;
+    }
+    scratch = t.ptr[dev];
+  }
+  return xm_qgemv(qtype, d_w, w_bytes, n, k, d_x, x_dtype, m, d_bias, d_y, scratch, kNoAllocScratchBytes, stream);
 }
