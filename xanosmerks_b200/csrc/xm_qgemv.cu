@@ -17,6 +17,7 @@
 //   in fp32.  Slower; it is the fallback and the cross-check.
 #include <algorithm>
 #include <mutex>
+#include <type_traits>
 
 #include "xm_qtypes.cuh"
 
@@ -57,7 +58,7 @@ __global__ void __launch_bounds__(kThreads) k_split_x(const XT* __restrict__ x, 
   float t = 0.f;
   if (amax > 0.f) {
     const float sc = amax / 127.0f;
-    const float u = v / sc;
+    const float u = v * (1.0f / sc);
     const float r0 = rintf(u);
     x0 = (int)r0;
     x1 = (int)rintf((u - r0) * 254.0f);
@@ -384,7 +385,13 @@ constexpr int kWsSlots = 11;
 constexpr int kWsRowsPerSlot = 4;
 constexpr int kRowBytes4096 = 16 * 144;
 constexpr int kWsSlotBytes = kWsRowsPerSlot * kRowBytes4096;
-constexpr int kWsSmem = kWsSlots * kWsSlotBytes + kLaneMajorBytes + (2 * kWsSlots + 1) * 8 + (kWsSlots + 1) * 4 + 16;
+// slots | lane-major split | barriers and counters | (fused form) the raw fp32/bf16 row of x
+// (barriers 23 x 8 B + counter + 11 slot tags = 232 B, rounded up so that the
+// row of x behind it keeps the 16-byte alignment a bulk copy needs)
+constexpr int kWsCtlBytes = 256;
+static_assert((2 * kWsSlots + 1) * 8 + (kWsSlots + 1) * 4 <= kWsCtlBytes, "control block");
+static_assert((kWsSlots * kWsSlotBytes + kLaneMajorBytes + kWsCtlBytes) % 16 == 0, "x row alignment");
+constexpr int kWsSmem = kWsSlots * kWsSlotBytes + kLaneMajorBytes + kWsCtlBytes + 4096 * 4;
 
 XM_DEV int dp4a_us(uint32_t a, uint32_t b, int c) {   // unsigned bytes of a x signed bytes of b
   int d;
@@ -427,8 +434,54 @@ XM_DEV float q4k_lane_dot(uint4 hd, uint4 q0, uint4 q1, uint4 q2, uint4 q3, int 
   return d * acc - dmin * macc;
 }
 
+// The activation split written by the consumer warps straight into the
+// lane-major shared-memory layout (the fused form of k_split_x for one row of
+// 4096).  Threads 0..255 work: thread t takes half (t&1) -- 16 elements -- of
+// 32-element group t>>1, so each thread writes whole 16-byte digit chunks and
+// the only cross-thread step is one shuffle for the group max and one for the
+// sum.  `x` is a shared-memory copy of the row.
+template <typename XT>
+XM_DEV void split_row4096_to_smem(const XT* x, uint8_t* xsm, int tid) {
+  if (tid >= 256) return;
+  const int g = tid >> 1, half = tid & 1;
+  float v[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) v[e] = to_f32(x[g * 32 + half * 16 + e]);
+  float amax = 0.f, s = 0.f;
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    amax = fmaxf(amax, fabsf(v[e]));
+    s += v[e];
+  }
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  const float s_other = __shfl_xor_sync(0xffffffffu, s, 1);
+  uint32_t w0[4] = {0, 0, 0, 0}, w1[4] = {0, 0, 0, 0};
+  float t = 0.f;
+  if (amax > 0.f) {
+    const float sc = amax / 127.0f;
+    const float inv = 1.0f / sc;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const float u = v[e] * inv;
+      const float r0 = rintf(u);
+      const int x0 = (int)r0;
+      const int x1 = max(-127, min(127, (int)rintf((u - r0) * 254.0f)));
+      w0[e >> 2] |= (uint32_t)(x0 & 0xFF) << (8 * (e & 3));
+      w1[e >> 2] |= (uint32_t)(x1 & 0xFF) << (8 * (e & 3));
+    }
+    t = sc / 254.0f;
+  }
+  const int L = g >> 2, i = g & 3;
+  *reinterpret_cast<uint4*>(xsm + ((4 * i + half) * 32 + L) * 16) = make_uint4(w0[0], w0[1], w0[2], w0[3]);
+  *reinterpret_cast<uint4*>(xsm + ((4 * i + 2 + half) * 32 + L) * 16) = make_uint4(w1[0], w1[1], w1[2], w1[3]);
+  if (half == 0) *reinterpret_cast<float2*>(xsm + 8192 + (32 * i + L) * 8) = make_float2(t, s + s_other);
+}
+
+// XT = void: the split comes from a workspace written by k_split_x (lane-major);
+// otherwise x itself is read and split in the prologue.
+template <typename XT>
 __global__ void __launch_bounds__(kWsThreads, 1) k_qgemv_q4k_k4096_m1(const uint8_t* __restrict__ W, int N,
-                                                                      const int8_t* __restrict__ pieces,
+                                                                      const void* __restrict__ xin,
                                                                       const float* __restrict__ bias,
                                                                       float* __restrict__ y) {
   extern __shared__ __align__(128) uint8_t ws_smem[];
@@ -477,12 +530,24 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_qgemv_q4k_k4096_m1(const uint
     return;
   }
 
-  grid_dep_wait();  // the activation split is produced by the preceding kernel
-  if (tid == 0) {
-    mbar_arrive_expect_tx(xbar, kLaneMajorBytes);
-    bulk_g2s(xsm, pieces, kLaneMajorBytes, xbar);
+  grid_dep_wait();  // x (or its split) is produced by the preceding kernel
+  if constexpr (std::is_same<XT, void>::value) {
+    if (tid == 0) {
+      mbar_arrive_expect_tx(xbar, kLaneMajorBytes);
+      bulk_g2s(xsm, xin, kLaneMajorBytes, xbar);
+    }
+    mbar_wait_bounded(xbar, 0);
+  } else {
+    // one bulk copy brings the whole row (8 KB bf16 / 16 KB fp32) in a single latency
+    XT* xrow = reinterpret_cast<XT*>(xsm + kLaneMajorBytes + kWsCtlBytes);
+    if (tid == 0) {
+      mbar_arrive_expect_tx(xbar, 4096 * sizeof(XT));
+      bulk_g2s(xrow, xin, 4096 * sizeof(XT), xbar);
+    }
+    mbar_wait_bounded(xbar, 0);
+    split_row4096_to_smem<XT>(xrow, xsm, tid);
+    asm volatile("bar.sync 1, %0;" ::"r"(kWsConsumers * 32) : "memory");   // consumer warps only
   }
-  mbar_wait_bounded(xbar, 0);
   const int c = lane >> 1, h = lane & 1;
   uint32_t xd[4][16];
   float tx[4], tw[4];
@@ -531,17 +596,19 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_qgemv_q4k_k4096_m1(const uint
   }
 }
 
-int launch_q4k_k4096_m1(const uint8_t* W, int64_t N, const int8_t* pieces, const float* bias, float* y,
+template <typename XT>
+int launch_q4k_k4096_m1(const uint8_t* W, int64_t N, const void* xin, const float* bias, float* y,
                         cudaStream_t st) {
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(k_qgemv_q4k_k4096_m1, cudaFuncAttributeMaxDynamicSharedMemorySize, kWsSmem);
+    cudaError_t e =
+        cudaFuncSetAttribute(k_qgemv_q4k_k4096_m1<XT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kWsSmem);
     if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemv: smem attribute: %s", cudaGetErrorString(e));
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
-  const int grid = (int)std::min<int64_t>(sm_count(), N);
+  const int grid = (int)std::min<int64_t>(sm_count(), (N + 1) / 2);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kWsThreads);
@@ -552,7 +619,7 @@ int launch_q4k_k4096_m1(const uint8_t* W, int64_t N, const int8_t* pieces, const
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k_qgemv_q4k_k4096_m1, W, (int)N, pieces, bias, y);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_qgemv_q4k_k4096_m1<XT>, W, (int)N, xin, bias, y);
   if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemv launch: %s", cudaGetErrorString(e));
   return XM_OK;
 }
@@ -775,7 +842,7 @@ int gemv_presplit(int qtype, const uint8_t* W, int64_t n, int64_t k, int64_t m, 
   const int64_t nb = k / 256;
   (void)qtype;
   if (lane_major_shape(m, k)) {
-    const int rc = launch_q4k_k4096_m1(W, n, pieces, bias, y, st);
+    const int rc = launch_q4k_k4096_m1<void>(W, n, pieces, bias, y, st);
     if (rc) return rc;
     return xm_check_launch("qgemv(integer, k4096 m1)");
   }
@@ -870,6 +937,17 @@ extern "C" int xm_qgemv(int qtype, const void* d_w, int64_t w_bytes, int64_t n, 
   cudaStream_t st = (cudaStream_t)stream;
   const bool fast = integer_path_type(qtype) && ((uintptr_t)d_w & 15) == 0 && d_workspace &&
                     workspace_bytes >= xm_qgemv_workspace_size(k, m) && ((uintptr_t)d_workspace & 15) == 0;
+  if (integer_path_type(qtype) && lane_major_shape(m, k) && ((uintptr_t)d_w & 15) == 0) {
+    // one row of 4096: the split is done inside the GEMV, no workspace needed
+    if (x_dtype == XM_DT_F32)
+      rc = launch_q4k_k4096_m1<float>((const uint8_t*)d_w, n, d_x, d_bias, d_y, st);
+    else if (x_dtype == XM_DT_BF16)
+      rc = launch_q4k_k4096_m1<__nv_bfloat16>((const uint8_t*)d_w, n, d_x, d_bias, d_y, st);
+    else
+      rc = launch_q4k_k4096_m1<__half>((const uint8_t*)d_w, n, d_x, d_bias, d_y, st);
+    if (rc) return rc;
+    return xm_check_launch("qgemv(integer, k4096 m1, fused split)");
+  }
   if (fast) {
     rc = split_activation(d_x, x_dtype, m, k, d_workspace, st);
     if (rc) return rc;
