@@ -56,6 +56,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the prefill (tensor-core GEMM) sweep")
+    ap.add_argument("--gemm-m", type=int, default=0,
+                    help="only time the prefill GEMM with this many activation rows (profiling mode)")
     return ap.parse_args()
 
 
@@ -201,6 +204,12 @@ def run_ours(args):
     lib = _lib.lib
     qid = 12
 
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
     raw = make_weight(QTYPE, N, K, seed=rank)
     w0 = torch.from_numpy(raw).to(dev)
     ws = [w0] + [w0.clone() for _ in range(COPIES - 1)]
@@ -264,6 +273,34 @@ def run_ours(args):
     torch.cuda.synchronize()
     err = float((y - y_exact).abs().max() / y_exact.abs().max())
 
+    # prefill sweep of the same weight (tensor-core dequant-GEMM): TFLOPS per M
+    sweep = {}
+    if not args.no_sweep:
+        for mm in (64, 512, 2048):
+            xs = torch.from_numpy(np.random.default_rng(5).standard_normal((mm, K)).astype(np.float32)).to(dev).to(
+                torch.bfloat16)
+            ys = torch.empty((mm, N), dtype=torch.float32, device=dev)
+            gsz = lib.xm_qgemm_workspace_size(mm, K)
+            gws = torch.empty(gsz, dtype=torch.uint8, device=dev)
+
+            def gstep(i, xs=xs, ys=ys, gws=gws, gsz=gsz, mm=mm):
+                w = ws[i % COPIES]
+                _lib.check(lib.xm_qgemm(qid, w.data_ptr(), W_BYTES, N, K, xs.data_ptr(), _lib.DT_BF16, mm, None,
+                                        ys.data_ptr(), gws.data_ptr(), gsz,
+                                        torch.cuda.current_stream().cuda_stream), "qgemm")
+            reps = 50 if mm <= 512 else 20
+            for i in range(3):
+                gstep(i)
+            g = capture(gstep, reps)
+            g.replay()
+            torch.cuda.synchronize()
+            ms = timed(g)
+            del g
+            flops = 2.0 * mm * N * K
+            tf = flops * reps / (ms / 1e3) / 1e12
+            sweep[f"M={mm}"] = {"TFLOPS": round(tf, 1), "us": round(ms * 1e3 / reps, 2),
+                                "frac_of_measured_bf16_peak": round(tf / float(peaks.get("bf16_tflops", 1590.0)), 4)}
+
     # end to end through the public API: pinned host activation in, fp32 result back to host, every step
     ops = [LinearOp(GGUFTensor(w, QTYPE, (N, K))) for w in ws]
     x_pin = torch.from_numpy(xb).to(torch.bfloat16).pin_memory()
@@ -288,12 +325,6 @@ def run_ours(args):
            "ms_per_step": round(t_e2e / e2e_steps * 1e3, 4)}
 
     value = world * args.steps * W_BYTES / (ms_steps / 1e3) / 1e9
-    peaks = {}
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            peaks = json.load(f)
-    except OSError:
-        pass
     peak = float(peaks.get("hbm_gbs", 6650.0))
     peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
     alg_bytes = W_BYTES + M * K * 2 + M * N * 4          # blocks + bf16 x + fp32 y
@@ -316,7 +347,9 @@ def run_ours(args):
                "warmup": args.warmup, "ms_per_step": round(ms_steps / args.steps, 6), "higher_is_better": True,
                "scaling": "weak", "vs_baseline": None, "dtype": "i32 dp4a + f32", "data": "synthetic",
                "config": config({"max_rel_err_vs_exact_path": err}), "e2e": e2e, "roofline": roofline,
-               "cpu_baseline": cpu, "clocks": clocks, "gpu_launches": args.steps}
+               "cpu_baseline": cpu, "clocks": clocks, "gpu_launches": args.steps,
+               "prefill_sweep": {"metric": f"{QTYPE} {N}x{K} dequant-GEMM TFLOPS (bf16 x, fp16-exact weights)",
+                                 "points": sweep}}
         print(json.dumps(out), flush=True)
     del g_steps
     if world > 1:
@@ -324,8 +357,41 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_gemm_only(args):
+    """One prefill GEMM shape, timed alone (the mode ncu captures use)."""
+    import torch
+    from xanosmerks_b200 import _lib
+    from xanosmerks_b200.synth import make_weight
+    lib = _lib.lib
+    dev = torch.device("cuda", 0)
+    w = torch.from_numpy(make_weight(QTYPE, N, K, seed=0)).to(dev)
+    mm = args.gemm_m
+    xs = torch.from_numpy(np.random.default_rng(5).standard_normal((mm, K)).astype(np.float32)).to(dev).to(torch.bfloat16)
+    ys = torch.empty((mm, N), dtype=torch.float32, device=dev)
+    gsz = lib.xm_qgemm_workspace_size(mm, K)
+    gws = torch.empty(gsz, dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream().cuda_stream
+    for _ in range(args.warmup):
+        _lib.check(lib.xm_qgemm(12, w.data_ptr(), W_BYTES, N, K, xs.data_ptr(), _lib.DT_BF16, mm, None,
+                                ys.data_ptr(), gws.data_ptr(), gsz, st), "qgemm")
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        _lib.check(lib.xm_qgemm(12, w.data_ptr(), W_BYTES, N, K, xs.data_ptr(), _lib.DT_BF16, mm, None,
+                                ys.data_ptr(), gws.data_ptr(), gsz, st), "qgemm")
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    print(json.dumps({"gemm_m": mm, "n": N, "k": K, "us": round(us, 2),
+                      "TFLOPS": round(2.0 * mm * N * K / us / 1e6, 1)}), flush=True)
+
+
 def main():
     args = parse()
+    if args.gemm_m:
+        run_gemm_only(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

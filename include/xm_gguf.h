@@ -110,6 +110,25 @@ int xm_qgemv_exact(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64
                    void* stream);
 
 /*
+ * Prefill GEMM on 5th-generation tensor cores: y[m][n] = sum_k x[m][k] *
+ * W[n][k] (+ bias[n]) for any m >= 1 (meant for m >= 64), x row-major [m][k]
+ * of x_dtype (16-byte aligned), y row-major [m][n] fp32.  Each weight is
+ * decoded to the reference's fp16 value, x is converted to fp16 with an exact
+ * power-of-two scale per row, tcgen05.mma accumulates in fp32: the result
+ * differs from the reference's fp32 `x @ W.T` only in summation order.
+ * `d_workspace` (256-byte aligned, >= xm_qgemm_workspace_size(m, k) bytes)
+ * holds the converted activations.  Types other than Q4_K return
+ * XM_ERR_UNSUPPORTED (callers fall back to xm_qgemv on row groups).
+ *
+ * Replaces the prefill `x @ W.T` of LinearOp.forward (ops.py:62-67) and of
+ * the MLP / attention projections (forward.py:93-101, attention.py:47-51).
+ */
+int64_t xm_qgemm_workspace_size(int64_t m, int64_t k);
+int xm_qgemm(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k,
+             const void* d_x, int x_dtype, int64_t m, const float* d_bias, float* d_y,
+             void* d_workspace, int64_t workspace_bytes, void* stream);
+
+/*
  * xm_qgemv without a workspace argument, for callers that cannot allocate
  * device memory (a host runtime that owns the allocator, a process that must
  * not allocate after start-up).  The activation split lives in a fixed array

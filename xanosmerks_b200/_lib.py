@@ -35,6 +35,8 @@ SIGNATURES = {
     "xm_qgemv_exact": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _int, _i64, _vp, _vp, _vp]),
     "xm_split_activation": (_int, [_vp, _int, _i64, _i64, _vp, _i64, _vp]),
     "xm_qgemv_presplit": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp]),
+    "xm_qgemm_workspace_size": (_i64, [_i64, _i64]),
+    "xm_qgemm": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _int, _i64, _vp, _vp, _vp, _i64, _vp]),
     "xm_qgemv_noalloc": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _int, _i64, _vp, _vp, _vp]),
 }
 

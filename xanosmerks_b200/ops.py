@@ -22,6 +22,8 @@ from .gguf_dequant import dequantize_device
 __all__ = ["GGUFTensor", "LinearOp", "FusedRMSNormLinearOp", "qlinear"]
 
 _DT = {torch.float32: DT_F32, torch.bfloat16: DT_BF16, torch.float16: DT_F16}
+# block types with a tensor-core GEMM for m > 8 (others use the GEMV on groups of 8 rows)
+_TC_TYPES = {"Q4_K"}
 
 
 class GGUFTensor:
@@ -97,6 +99,13 @@ def qlinear(weight: GGUFTensor, x: torch.Tensor, bias: torch.Tensor | None = Non
         b = bias.to(device=x.device, dtype=torch.float32).contiguous()
     stream = torch.cuda.current_stream(x.device).cuda_stream
     with torch.cuda.device(x.device):
+        if m > 8 and not exact and weight.qtype.name in _TC_TYPES:
+            wsz = lib.xm_qgemm_workspace_size(m, k)
+            ws = _workspace(x.device, wsz)
+            check(lib.xm_qgemm(weight.qtype.type_id, weight.data.data_ptr(), weight.nbytes, n, k, x2.data_ptr(),
+                               _DT[x2.dtype], m, b.data_ptr() if b is not None else None, y.data_ptr(),
+                               ws.data_ptr(), ws.numel(), stream), "qgemm")
+            return y.reshape(*lead, n)
         for m0 in range(0, m, 8):
             mm = min(8, m - m0)
             xs = x2[m0:m0 + mm]
