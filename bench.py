@@ -376,15 +376,16 @@ def run_gemm_only(args):
                                 ys.data_ptr(), gws.data_ptr(), gsz, st), "qgemm")
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        _lib.check(lib.xm_qgemm(12, w.data_ptr(), W_BYTES, N, K, xs.data_ptr(), _lib.DT_BF16, mm, None,
-                                ys.data_ptr(), gws.data_ptr(), gsz, st), "qgemm")
-    e1.record()
-    torch.cuda.synchronize()
+    with Clocks(0) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            _lib.check(lib.xm_qgemm(12, w.data_ptr(), W_BYTES, N, K, xs.data_ptr(), _lib.DT_BF16, mm, None,
+                                    ys.data_ptr(), gws.data_ptr(), gsz, st), "qgemm")
+        e1.record()
+        torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / args.steps
     print(json.dumps({"gemm_m": mm, "n": N, "k": K, "us": round(us, 2),
-                      "TFLOPS": round(2.0 * mm * N * K / us / 1e6, 1)}), flush=True)
+                      "TFLOPS": round(2.0 * mm * N * K / us / 1e6, 1), "clocks": clk.summary()}), flush=True)
 
 
 def main():

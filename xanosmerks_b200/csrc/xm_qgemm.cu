@@ -14,15 +14,17 @@
 // rounding).
 //
 // Structure (one CTA per output tile of MT*128 rows x BN columns):
-//   warp 0      TMA producer: activation tiles (fp16, 128-byte swizzle, 2-D
-//               tensor map) and raw Q4_K super-blocks (BN rows x 144 B per
-//               super-block column, 2-D tensor map over the byte stream); no
-//               multicast anywhere.
+//   warp 0      TMA producer of the activation tiles (fp16, 128-byte swizzle,
+//               2-D tensor map, no multicast).
 //   warp 1      allocates tensor memory and issues tcgen05.mma (one thread).
-//   warps 2-9   decode the raw super-block into the fp16 B tile of each
+//   warps 2-17  decode the weight blocks into the fp16 B tile of each
 //               64-wide K step, written straight into the UMMA K-major
-//               128-byte-swizzled layout; afterwards they run the epilogue
-//               (tcgen05.ld -> row scale -> y).
+//               128-byte-swizzled layout.  The blocks are read from global
+//               memory (the whole quantized matrix stays L2-resident across
+//               the M tiles) one K step ahead into registers; one thread
+//               decodes one 32-weight sub-block of one row per item with
+//               packed fp32x2 arithmetic.  Afterwards these warps run the
+//               epilogue (tcgen05.ld -> row scale -> y).
 // Pipelines are mbarrier rings with bounded waits.
 #include <cuda.h>
 
@@ -33,10 +35,10 @@
 
 namespace {
 
-constexpr int kStages = 3;
+constexpr int kMaxStages = 8;                  // ring depth: as many stages as shared memory holds
 constexpr int kBK = 64;                        // K elements per stage (one 128-byte swizzle atom of fp16)
 constexpr int kATileBytes = 128 * kBK * 2;     // one 128-row A box
-constexpr int kDequantWarps = 8;
+constexpr int kDequantWarps = 16;
 constexpr int kThreads = (2 + kDequantWarps) * 32;
 
 XM_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -62,9 +64,18 @@ XM_DEV void tc_commit(uint64_t* bar) {
 XM_DEV void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}"
-      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+// Wait for an mbarrier phase, testing once without suspending first (the
+// common case on the MMA thread is that the stage is already full).
+XM_DEV void mbar_wait_fast(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+               : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  if (!ok) mbar_wait_bounded(bar, parity);
 }
 
 XM_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
@@ -72,6 +83,16 @@ XM_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+XM_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
 XM_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
@@ -133,26 +154,77 @@ __global__ void __launch_bounds__(256) k_prep_rows(const XT* __restrict__ x, int
 // The GEMM kernel.
 // ---------------------------------------------------------------------------
 struct GemmSmem {
-  uint64_t a_full[kStages], b_full[kStages], ab_empty[kStages];
-  uint64_t raw_full[2], raw_empty[2];
+  uint64_t full[kMaxStages], ab_empty[kMaxStages];   // full: A bytes + one arrival per decode warp
   uint64_t acc_full;
   uint32_t tmem_base;
 };
 
+// One decode item: 32 weights (sub-block 2j+h of row n in K step kt) as raw bytes.
+struct RawItem {
+  uint4 hd;        // d, dmin, 12 scale bytes
+  uint4 q0, q1;    // the 32 qs bytes of sub-block pair j
+};
+
+XM_DEV RawItem load_item(const uint8_t* W, int64_t row_bytes, int n, int N, int kt) {
+  RawItem it;
+  const int nn = n < N ? n : N - 1;                    // rows past N decode a valid row; the epilogue drops them
+  const uint8_t* blk = W + (int64_t)nn * row_bytes + (int64_t)(kt >> 2) * 144;
+  const int j = kt & 3;
+  it.hd = ldg_stream_v4(blk);
+  it.q0 = ldg_stream_v4(blk + 16 + 32 * j);
+  it.q1 = ldg_stream_v4(blk + 32 + 32 * j);
+  return it;
+}
+
+// Decode one item into fp16 and store its 4 chunks into the swizzled B row.
+XM_DEV void decode_item(const RawItem& it, int h, int j, uint8_t* row, int n) {
+  const uint32_t A = it.hd.y, B = it.hd.z, C = it.hd.w;
+  const int sub = 2 * j + h;
+  const uint32_t scw = sub < 4 ? (A & 0x3F3F3F3Fu) : ((C & 0x0F0F0F0Fu) | ((A >> 2) & 0x30303030u));
+  const uint32_t mnw = sub < 4 ? (B & 0x3F3F3F3Fu) : (((C >> 4) & 0x0F0F0F0Fu) | ((B >> 2) & 0x30303030u));
+  const float d = __half2float(__ushort_as_half((unsigned short)(it.hd.x & 0xFFFF)));
+  const float dmin = __half2float(__ushort_as_half((unsigned short)(it.hd.x >> 16)));
+  const float d1 = __fmul_rn(d, byte_f(scw, sub & 3));       // exact (11-bit x 6-bit)
+  const float m1 = __fmul_rn(dmin, byte_f(mnw, sub & 3));
+  const float2 dd = make_float2(d1, d1), mm = make_float2(-m1, -m1), mg = make_float2(-8388608.0f, -8388608.0f);
+  const uint32_t qw[8] = {it.q0.x, it.q0.y, it.q0.z, it.q0.w, it.q1.x, it.q1.y, it.q1.z, it.q1.w};
+  const int sh = 4 * h;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {           // chunk c: weights 8c .. 8c+7 of the sub-block
+    uint32_t hv[4];
+#pragma unroll
+    for (int wv = 0; wv < 2; ++wv) {
+      const uint32_t nib = (qw[2 * c + wv] >> sh) & 0x0F0F0F0Fu;
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        // 2^23 + q as floats (magic exponent), minus 2^23: exact small integers
+        float2 q = make_float2(__uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7650u | (2 * p))),
+                               __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7650u | (2 * p + 1))));
+        q = __fadd2_rn(q, mg);
+        // d1*q is exact, so one rounding of d1*q - m1 is the reference's fp32 value
+        const float2 v = __ffma2_rn(dd, q, mm);
+        const __half2 hh = __floats2half2_rn(v.x, v.y);
+        hv[2 * wv + p] = *reinterpret_cast<const uint32_t*>(&hh);
+      }
+    }
+    const int chunk = 4 * h + c;
+    *reinterpret_cast<uint4*>(row + ((chunk ^ (n & 7)) << 4)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+  }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
-    k_qgemm_q4k_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w, int M, int N,
-                   int K, int MT, int BN, const float* __restrict__ rowscale, const float* __restrict__ bias,
-                   float* __restrict__ y) {
+    k_qgemm_q4k_tc(const __grid_constant__ CUtensorMap map_a, const uint8_t* __restrict__ W, int M, int N,
+                   int K, int MT, int BN, int kStages, const float* __restrict__ rowscale,
+                   const float* __restrict__ bias, float* __restrict__ y) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  // 1024-byte aligned carve-up: A stages | B stages | raw W (x2) | control
+  // 1024-byte aligned carve-up: A stages | B stages | control
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int a_stage_bytes = MT * kATileBytes;
   const int b_stage_bytes = BN * kBK * 2;
-  const int raw_bytes = BN * 144;
   uint8_t* sA = base;
   uint8_t* sB = sA + kStages * a_stage_bytes;
-  uint8_t* sRaw = sB + kStages * b_stage_bytes;
-  GemmSmem* ctl = reinterpret_cast<GemmSmem*>(sRaw + ((2 * raw_bytes + 15) & ~15));
+  GemmSmem* ctl = reinterpret_cast<GemmSmem*>(sB + kStages * b_stage_bytes);
+  const int64_t row_bytes = (int64_t)(K / 256) * 144;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n0 = blockIdx.x * BN;
@@ -161,13 +233,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     for (int i = 0; i < kStages; ++i) {
-      mbar_init(&ctl->a_full[i], 1);
-      mbar_init(&ctl->b_full[i], kDequantWarps);
+      mbar_init(&ctl->full[i], 1 + kDequantWarps);
       mbar_init(&ctl->ab_empty[i], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&ctl->raw_full[i], 1);
-      mbar_init(&ctl->raw_empty[i], kDequantWarps);
     }
     mbar_init(&ctl->acc_full, 1);
     fence_mbar_init();
@@ -190,113 +257,95 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       grid_dep_wait();   // the prepared activation comes from the preceding kernel
       for (int kt = 0; kt < nkt; ++kt) {
-        if ((kt & 3) == 0) {
-          const int sb = kt >> 2, r = sb & 1;
-          if (sb >= 2) mbar_wait_bounded(&ctl->raw_empty[r], (uint32_t)(((sb >> 1) - 1) & 1));
-          mbar_arrive_expect_tx(&ctl->raw_full[r], (uint32_t)raw_bytes);
-          tma_load_2d(sRaw + r * raw_bytes, &map_w, sb * 144, n0, &ctl->raw_full[r]);
-        }
         const int s = kt % kStages;
         if (kt >= kStages) mbar_wait_bounded(&ctl->ab_empty[s], (uint32_t)(((kt / kStages) - 1) & 1));
-        mbar_arrive_expect_tx(&ctl->a_full[s], (uint32_t)a_stage_bytes);
+        mbar_arrive_expect_tx(&ctl->full[s], (uint32_t)a_stage_bytes);
         for (int mt = 0; mt < MT; ++mt)
-          tma_load_2d(sA + s * a_stage_bytes + mt * kATileBytes, &map_a, kt * kBK, m0 + mt * 128, &ctl->a_full[s]);
+          tma_load_2d(sA + s * a_stage_bytes + mt * kATileBytes, &map_a, kt * kBK, m0 + mt * 128, &ctl->full[s]);
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       const uint32_t idesc = idesc_f16_f32(BN);
+      // descriptors of stage 0; stage s and K sub-step kk only move the start
+      // address (16-byte units): + s*stage_bytes/16 + kk*2
+      const uint64_t a0 = smem_desc_sw128(sA), b0 = smem_desc_sw128(sB);
+      int s = 0;
+      uint32_t ph = 0;
       for (int kt = 0; kt < nkt; ++kt) {
-        const int s = kt % kStages;
-        const uint32_t ph = (uint32_t)((kt / kStages) & 1);
-        mbar_wait_bounded(&ctl->a_full[s], ph);
-        mbar_wait_bounded(&ctl->b_full[s], ph);
+        mbar_wait_fast(&ctl->full[s], ph);
         tc_fence_after();
-        const uint8_t* a = sA + s * a_stage_bytes;
-        const uint8_t* b = sB + s * b_stage_bytes;
+        const uint64_t as = a0 + (uint64_t)((s * a_stage_bytes) >> 4);
+        const uint64_t bs = b0 + (uint64_t)((s * b_stage_bytes) >> 4);
         for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t ad = smem_desc_sw128(a + mt * kATileBytes + kk * 32);
-            const uint64_t bd = smem_desc_sw128(b + kk * 32);
-            tc_mma_f16(tmem + (uint32_t)(mt * BN), ad, bd, idesc, (kt | kk) != 0 ? 1u : 0u);
-          }
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            tc_mma_f16(tmem + (uint32_t)(mt * BN), as + (uint64_t)((mt * kATileBytes) >> 4) + 2 * kk, bs + 2 * kk,
+                       idesc, (kt | kk) != 0 ? 1u : 0u);
         }
         tc_commit(&ctl->ab_empty[s]);   // frees the stage once these MMAs have read it
+        if (++s == kStages) { s = 0; ph ^= 1u; }
       }
       tc_commit(&ctl->acc_full);
     }
   } else {
     // ---------------- dequant producers ----------------
-    const int dw = warp - 2;                     // 0..7
-    const int dt = dw * 32 + lane;               // 0..255
-    const int items = BN * 4;                    // (row, 16-element quarter) per K step
-    for (int kt = 0; kt < nkt; ++kt) {
-      const int sb = kt >> 2, j = kt & 3, r = sb & 1;
-      if (j == 0) mbar_wait_bounded(&ctl->raw_full[r], (uint32_t)((sb >> 1) & 1));
-      const int s = kt % kStages;
-      if (kt >= kStages) mbar_wait_bounded(&ctl->ab_empty[s], (uint32_t)(((kt / kStages) - 1) & 1));
-      const uint8_t* raw = sRaw + r * raw_bytes;
-      uint8_t* bt = sB + s * b_stage_bytes;
-      for (int it = dt; it < items; it += kDequantWarps * 32) {
-        const int n = it >> 2, qd = it & 3;      // elements 16*qd .. 16*qd+15 of this K step
-        const uint8_t* blk = raw + n * 144;
-        const uint32_t hw = *reinterpret_cast<const uint32_t*>(blk);
-        const uint32_t A = *reinterpret_cast<const uint32_t*>(blk + 4);
-        const uint32_t B = *reinterpret_cast<const uint32_t*>(blk + 8);
-        const uint32_t C = *reinterpret_cast<const uint32_t*>(blk + 12);
-        const int sub = 2 * j + (qd >> 1);       // sub-block 2j (low nibbles) or 2j+1 (high)
-        const uint32_t scw = sub < 4 ? (A & 0x3F3F3F3Fu) : ((C & 0x0F0F0F0Fu) | ((A >> 2) & 0x30303030u));
-        const uint32_t mnw = sub < 4 ? (B & 0x3F3F3F3Fu) : (((C >> 4) & 0x0F0F0F0Fu) | ((B >> 2) & 0x30303030u));
-        const float d = __half2float(__ushort_as_half((unsigned short)(hw & 0xFFFF)));
-        const float dmin = __half2float(__ushort_as_half((unsigned short)(hw >> 16)));
-        const float d1 = __fmul_rn(d, byte_f(scw, sub & 3));
-        const float m1 = __fmul_rn(dmin, byte_f(mnw, sub & 3));
-        const uint4 qv = *reinterpret_cast<const uint4*>(blk + 16 + 32 * j + 16 * (qd & 1));
-        const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
-        const int sh = (qd >> 1) * 4;
-        uint32_t h[8];
+    const int dt = (warp - 2) * 32 + lane;       // 0..511: one item (row dt/2, half dt&1) per K step
+    const int h = dt & 1;
+    const int n = dt >> 1;
+    const bool active = n < BN;
+    // block bytes are prefetched kPre K steps ahead into a register ring
+    // (the loads come from L2; one step of lookahead left the warps waiting)
+    constexpr int kPre = 3;
+    RawItem ring[kPre];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const uint32_t w = qw[t >> 1] >> (16 * (t & 1));          // bytes 2t, 2t+1 of the 16
-          const float q0 = (float)((w >> sh) & 15u), q1 = (float)((w >> (8 + sh)) & 15u);
-          const __half2 hv = __floats2half2_rn(__fsub_rn(__fmul_rn(d1, q0), m1), __fsub_rn(__fmul_rn(d1, q1), m1));
-          h[t] = *reinterpret_cast<const uint32_t*>(&hv);
+    for (int u = 0; u < kPre; ++u)
+      if (u < nkt && active) ring[u] = load_item(W, row_bytes, n0 + n, N, u);
+    for (int kt0 = 0; kt0 < nkt; kt0 += kPre) {
+#pragma unroll
+      for (int u = 0; u < kPre; ++u) {
+        const int kt = kt0 + u;
+        if (kt < nkt) {
+          const RawItem cur = ring[u];
+          if (kt + kPre < nkt && active) ring[u] = load_item(W, row_bytes, n0 + n, N, kt + kPre);
+          const int s = kt % kStages;
+          if (kt >= kStages) mbar_wait_bounded(&ctl->ab_empty[s], (uint32_t)(((kt / kStages) - 1) & 1));
+          if (active) decode_item(cur, h, kt & 3, sB + s * b_stage_bytes + n * 128, n);
+          fence_proxy_async_smem();    // generic-proxy writes -> visible to the tensor core
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ctl->full[s]);
         }
-        // K-major 128-byte swizzle: row n, 16-byte chunk c stored at chunk c ^ (n & 7)
-        uint8_t* row = bt + n * 128;
-        const int c0 = 2 * qd, c1 = 2 * qd + 1;
-        *reinterpret_cast<uint4*>(row + ((c0 ^ (n & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<uint4*>(row + ((c1 ^ (n & 7)) << 4)) = make_uint4(h[4], h[5], h[6], h[7]);
-      }
-      fence_proxy_async_smem();    // generic-proxy writes -> visible to the tensor core
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&ctl->b_full[s]);
-        if (j == 3) mbar_arrive(&ctl->raw_empty[r]);
       }
     }
     // ---------------- epilogue ----------------
+    // tcgen05.ld gives each lane 32 consecutive columns of its own row; a
+    // per-warp padded shared-memory tile turns that into row-contiguous
+    // 128-byte stores (lane-per-row stores scattered 4 bytes over 32 rows and
+    // held every CTA on its SM for tens of microseconds while they drained).
     mbar_wait_bounded(&ctl->acc_full, 0);
     tc_fence_after();
     const int sp = warp & 3;                     // TMEM sub-partition this warp may read
-    const int half = (warp - 2) >> 2;            // two warps per sub-partition split the columns
-    const int nchunks = BN / 16;
+    const int quarter = (warp - 2) >> 2;         // four warps per sub-partition split the columns
+    float* tile = reinterpret_cast<float*>(sA) + (warp - 2) * (32 * 33);   // operand stages are free now
+    const int nchunks = BN / 32;
     for (int mt = 0; mt < MT; ++mt) {
-      const int m = m0 + mt * 128 + sp * 32 + lane;
-      const float rs = m < M ? rowscale[m] : 0.f;
-      for (int ch = half; ch < nchunks; ch += 2) {
-        uint32_t v[16];
-        tmem_ld16(tmem + ((uint32_t)(sp * 32) << 16) + (uint32_t)(mt * BN + ch * 16), v);
+      const int mrow0 = m0 + mt * 128 + sp * 32;
+      for (int ch = quarter; ch < nchunks; ch += 4) {
+        uint32_t v[32];
+        tmem_ld32(tmem + ((uint32_t)(sp * 32) << 16) + (uint32_t)(mt * BN + ch * 32), v);
         tmem_ld_wait();
-        const int nn = n0 + ch * 16;
-        if (m < M) {
-          float* yr = y + (int64_t)m * N + nn;
+        const float rs = (mrow0 + lane) < M ? rowscale[mrow0 + lane] : 0.f;
 #pragma unroll
-          for (int t = 0; t < 16; ++t)
-            if (nn + t < N) yr[t] = __uint_as_float(v[t]) * rs + (bias ? bias[nn + t] : 0.f);
+        for (int t = 0; t < 32; ++t) tile[lane * 33 + t] = __uint_as_float(v[t]) * rs;
+        __syncwarp();
+        const int nn = n0 + ch * 32 + lane;
+        const float bv = (bias && nn < N) ? bias[nn] : 0.f;
+        for (int r = 0; r < 32; ++r) {
+          const int m = mrow0 + r;
+          if (m < M && nn < N) y[(int64_t)m * N + nn] = tile[r * 33 + lane] + bv;
         }
+        __syncwarp();
       }
     }
   }
@@ -336,30 +385,27 @@ int sm_count_dev() {
 }
 
 struct TileCfg {
-  int MT, BN;
+  int MT, BN, stages;
 };
 
-// Output tile shape: MT*128 rows x BN columns (BN a multiple of 16, MT*BN <=
-// 512 tensor-memory columns), picked to minimise the estimated makespan
-// (waves of tiles over the SMs, each tile's MMA and decode work) with a
-// penalty for re-reading x once per column tile.
+int stages_for(int MT, int BN) {
+  const int per = MT * kATileBytes + BN * kBK * 2;
+  const int avail = 227 * 1024 - 1024 - (int)sizeof(GemmSmem);
+  return std::max(2, std::min(kMaxStages, avail / per));
+}
+
+// Output tile shape: MT*128 rows x BN columns.  MT = 2 once there are 256
+// rows (each decoded B tile then serves 256 activation rows; MT*BN <= 512
+// tensor-memory columns), and BN (a multiple of 16, <= 256) as large as the
+// SM count allows: the activation is re-read once per column tile.
 TileCfg choose_tile(int64_t M, int64_t N, int64_t K, int sms) {
-  TileCfg best{1, 128};
-  double best_t = 1e30;
-  for (int MT = 1; MT <= 2; ++MT)
-    for (int BN = 32; BN <= 256; BN += 16) {
-      if (MT * BN > 512) continue;
-      const int64_t a_stage = (int64_t)MT * kATileBytes, b_stage = (int64_t)BN * kBK * 2;
-      if (kStages * (a_stage + b_stage) + 2 * BN * 144 + 1024 + 256 > 227 * 1024) continue;
-      const int64_t tn = (N + BN - 1) / BN, tm = (M + MT * 128 - 1) / (MT * 128);
-      const int64_t tiles = tn * tm;
-      const int64_t waves = (tiles + sms - 1) / sms;
-      const double mma = (double)MT * 128 * BN * K;            // MACs per tile
-      const double deq = (double)BN * K * 6.0;                 // decode work per tile (MAC-equivalents)
-      const double t = waves * std::max(mma / 4096.0, deq / 64.0) + (double)tn * M * K * 2 / 8e4;
-      if (t < best_t) { best_t = t; best = {MT, BN}; }
-    }
-  return best;
+  (void)K;
+  const int MT = M > 128 ? 2 : 1;
+  const int64_t tm = (M + MT * 128 - 1) / (MT * 128);
+  int64_t bn = (N * tm + sms - 1) / sms;                  // one wave if possible
+  bn = (bn + 31) / 32 * 32;                               // the epilogue moves 32-column chunks
+  bn = std::max<int64_t>(64, std::min<int64_t>(256, bn));
+  return {MT, (int)bn, stages_for(MT, (int)bn)};
 }
 
 }  // namespace
@@ -405,7 +451,7 @@ extern "C" int xm_qgemm(int qtype, const void* d_w, int64_t w_bytes, int64_t n, 
   if (rc) return rc;
 
   const TileCfg cfg = choose_tile(m, n, k, sm_count_dev());
-  CUtensorMap map_a, map_w;
+  CUtensorMap map_a;
   {
     const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
     const cuuint64_t strides[1] = {(cuuint64_t)k * 2};
@@ -416,18 +462,7 @@ extern "C" int xm_qgemm(int qtype, const void* d_w, int64_t w_bytes, int64_t n, 
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return xm_set_error(XM_ERR_CUDA, "qgemm: activation tensor map (%d)", (int)r);
   }
-  {
-    const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)n};
-    const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
-    const cuuint32_t box[2] = {144, (cuuint32_t)cfg.BN};
-    const cuuint32_t es[2] = {1, 1};
-    CUresult r = encode(&map_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(d_w), dims, strides, box, es,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return xm_set_error(XM_ERR_CUDA, "qgemm: weight tensor map (%d)", (int)r);
-  }
-  const int smem = 1024 + kStages * (cfg.MT * kATileBytes + cfg.BN * kBK * 2) + ((2 * cfg.BN * 144 + 15) & ~15) +
-                   (int)sizeof(GemmSmem);
+  const int smem = 1024 + cfg.stages * (cfg.MT * kATileBytes + cfg.BN * kBK * 2) + (int)sizeof(GemmSmem);
   cudaError_t e = cudaFuncSetAttribute(k_qgemm_q4k_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemm: smem attribute: %s", cudaGetErrorString(e));
   const dim3 grid((unsigned)((n + cfg.BN - 1) / cfg.BN), (unsigned)((m + cfg.MT * 128 - 1) / (cfg.MT * 128)));
@@ -441,7 +476,8 @@ extern "C" int xm_qgemm(int qtype, const void* d_w, int64_t w_bytes, int64_t n, 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = attr;
   lc.numAttrs = 1;
-  e = cudaLaunchKernelEx(&lc, k_qgemm_q4k_tc, map_a, map_w, (int)m, (int)n, (int)k, cfg.MT, cfg.BN,
+  e = cudaLaunchKernelEx(&lc, k_qgemm_q4k_tc, map_a, (const uint8_t*)d_w, (int)m, (int)n, (int)k, cfg.MT, cfg.BN,
+                         cfg.stages,
                          (const float*)rowscale, d_bias, d_y);
   if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemm launch: %s", cudaGetErrorString(e));
   return xm_check_launch("qgemm");
