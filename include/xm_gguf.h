@@ -129,6 +129,29 @@ int xm_qgemm(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k,
              void* d_workspace, int64_t workspace_bytes, void* stream);
 
 /*
+ * Sparse mixture-of-experts block (Mixtral-style SwiGLU experts):
+ *   out[t] = sum over the k experts e chosen for token t (ascending e) of
+ *            w[t][e] * ((silu(x_t @ W1_e.T) * (x_t @ W3_e.T)) @ W2_e.T)
+ * with router logits x @ gate.T (gate fp32 [E][H]), the k largest logits per
+ * token and a softmax over those k (over all E when k == E).  x row-major
+ * [T][H] of x_dtype, out fp32 [T][H].  h_w1/h_w3 ([F][H]) and h_w2 ([H][F])
+ * are HOST arrays of E device pointers to GGUF blocks of `qtype` (Q4_K; other
+ * types return XM_ERR_UNSUPPORTED).  E <= 32; H and F multiples of 256.
+ * `d_workspace` (256-byte aligned, xm_moe_workspace_size bytes) holds the
+ * routing, the gathered activations and the expert intermediates.  The whole
+ * block runs on `stream` without host synchronisation: routing, a stable
+ * counting sort by expert, grouped tensor-core GEMMs, fused SwiGLU, combine.
+ *
+ * Replaces moe.py:54-115 `MoELayer.__call__` (sparse top-k path and the
+ * dense k == E path).
+ */
+int64_t xm_moe_workspace_size(int64_t T, int64_t H, int64_t F, int E, int k);
+int xm_moe_forward(const void* d_x, int x_dtype, int64_t T, int64_t H, const float* d_gate,
+                   int E, int k, int64_t F, const void* const* h_w1, const void* const* h_w3,
+                   const void* const* h_w2, int qtype, float* d_out, void* d_workspace,
+                   int64_t workspace_bytes, void* stream);
+
+/*
  * xm_qgemv without a workspace argument, for callers that cannot allocate
  * device memory (a host runtime that owns the allocator, a process that must
  * not allocate after start-up).  The activation split lives in a fixed array

@@ -37,6 +37,9 @@ SIGNATURES = {
     "xm_qgemv_presplit": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp]),
     "xm_qgemm_workspace_size": (_i64, [_i64, _i64]),
     "xm_qgemm": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _int, _i64, _vp, _vp, _vp, _i64, _vp]),
+    "xm_moe_workspace_size": (_i64, [_i64, _i64, _i64, _int, _int]),
+    "xm_moe_forward": (_int, [_vp, _int, _i64, _i64, _vp, _int, _int, _i64, ctypes.POINTER(_vp),
+                              ctypes.POINTER(_vp), ctypes.POINTER(_vp), _int, _vp, _vp, _i64, _vp]),
     "xm_qgemv_noalloc": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _int, _i64, _vp, _vp, _vp]),
 }
 

@@ -1,0 +1,325 @@
+// K5/K6: sparse mixture-of-experts block on quantized expert weights.
+//
+// Mirrors moe.py:54-115 (MoELayer.__call__):
+//   router logits = x @ gate.T                     (moe.py:61)
+//   top-k experts per token, softmax over the k selected logits
+//                                                  (moe.py:75-81; dense softmax when k = E, moe.py:63-72)
+//   stable sort of the (token, slot) pairs by expert (moe.py:83-93)
+//   per expert: silu(x @ w1.T) * (x @ w3.T), then @ w2.T   (moe.py:97-113)
+//   output[token] += expert_out * weight, experts in ascending order (moe.py:112)
+//
+// Device pipeline (one stream, no host round trip):
+//   k_moe_router      one warp per token: E dot products, top-k, softmax
+//   k_moe_sort        one CTA: stable counting sort of the T*k pairs by expert
+//   k_moe_gather_prep gathered rows of x -> fp16 with a power-of-two row scale
+//   grouped GEMM      w1 and w3 over every expert's row range (tensor cores)
+//   k_swiglu_prep     silu(g) * u -> fp16 with row scale (A of the next GEMM)
+//   grouped GEMM      w2
+//   k_moe_combine     weighted sum of each token's k expert rows, ascending expert
+#include <algorithm>
+
+#include "xm_internal.h"
+#include "xm_qtypes.cuh"
+
+namespace {
+
+constexpr int kMaxExperts = 32;
+
+// primitives.py:7-11 softmax (max-shifted, + 1e-12 in the denominator)
+XM_DEV void softmax_small(float* v, int n) {
+  float mx = v[0];
+  for (int i = 1; i < n; ++i) mx = fmaxf(mx, v[i]);
+  if (!(fabsf(mx) < INFINITY)) mx = 0.f;
+  float s = 0.f;
+  for (int i = 0; i < n; ++i) {
+    v[i] = expf(v[i] - mx);
+    s += v[i];
+  }
+  for (int i = 0; i < n; ++i) v[i] = v[i] / (s + 1e-12f);
+}
+
+template <typename XT>
+__global__ void __launch_bounds__(256) k_moe_router(const XT* __restrict__ x, const float* __restrict__ gate, int T,
+                                                    int H, int E, int k, int* __restrict__ topk_e,
+                                                    float* __restrict__ topk_w) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (t >= T) return;
+  float acc[kMaxExperts];
+#pragma unroll
+  for (int e = 0; e < kMaxExperts; ++e) acc[e] = 0.f;
+  const XT* xr = x + (int64_t)t * H;
+  for (int h = lane; h < H; h += 32) {
+    const float xv = to_f32(xr[h]);
+#pragma unroll
+    for (int e = 0; e < kMaxExperts; ++e)
+      if (e < E) acc[e] = fmaf(xv, gate[(int64_t)e * H + h], acc[e]);
+  }
+#pragma unroll
+  for (int e = 0; e < kMaxExperts; ++e) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
+  }
+  if (lane != 0) return;
+  int sel[kMaxExperts];
+  float val[kMaxExperts];
+  if (k == E) {
+    for (int e = 0; e < E; ++e) { sel[e] = e; val[e] = acc[e]; }
+  } else {
+    bool used[kMaxExperts];
+    for (int e = 0; e < E; ++e) used[e] = false;
+    for (int j = 0; j < k; ++j) {       // the k largest logits (the set argpartition selects)
+      int best = -1;
+      for (int e = 0; e < E; ++e)
+        if (!used[e] && (best < 0 || acc[e] > acc[best])) best = e;
+      used[best] = true;
+      sel[j] = best;
+      val[j] = acc[best];
+    }
+  }
+  softmax_small(val, k);
+  for (int j = 0; j < k; ++j) {
+    topk_e[(int64_t)t * k + j] = sel[j];
+    topk_w[(int64_t)t * k + j] = val[j];
+  }
+}
+
+// Stable counting sort of P = T*k pairs by expert (one CTA of 1024 threads).
+__global__ void __launch_bounds__(1024) k_moe_sort(const int* __restrict__ topk_e, const float* __restrict__ topk_w,
+                                                   int P, int k, int E, int* __restrict__ sorted_tok,
+                                                   float* __restrict__ sorted_w, int* __restrict__ pair_pos,
+                                                   int* __restrict__ cnt, int* __restrict__ off) {
+  __shared__ int s_cnt[kMaxExperts], s_base[kMaxExperts], s_tot[kMaxExperts];
+  __shared__ int s_w[32][kMaxExperts];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid < kMaxExperts) s_cnt[tid] = 0;
+  __syncthreads();
+  for (int i = tid; i < P; i += 1024) atomicAdd(&s_cnt[topk_e[i]], 1);
+  __syncthreads();
+  if (tid == 0) {
+    int run = 0;
+    for (int e = 0; e < E; ++e) {
+      cnt[e] = s_cnt[e];
+      off[e] = run;
+      s_base[e] = run;
+      run += s_cnt[e];
+    }
+  }
+  __syncthreads();
+  const unsigned lt = (1u << lane) - 1u;
+  for (int c0 = 0; c0 < P; c0 += 1024) {
+    const int i = c0 + tid;
+    const int e = i < P ? topk_e[i] : -1;
+    int rank = 0;
+    for (int ex = 0; ex < E; ++ex) {
+      const unsigned b = __ballot_sync(0xffffffffu, e == ex);
+      if (lane == 0) s_w[warp][ex] = __popc(b);
+      if (e == ex) rank = __popc(b & lt);
+    }
+    __syncthreads();
+    if (tid < E) {                       // exclusive prefix over warps, per expert
+      int run = 0;
+      for (int w = 0; w < 32; ++w) {
+        const int c = s_w[w][tid];
+        s_w[w][tid] = run;
+        run += c;
+      }
+      s_tot[tid] = run;
+    }
+    __syncthreads();
+    if (i < P) {
+      const int pos = s_base[e] + s_w[warp][e] + rank;
+      sorted_tok[pos] = i / k;
+      sorted_w[pos] = topk_w[i];
+      pair_pos[i] = pos;
+    }
+    __syncthreads();
+    if (tid < E) s_base[tid] += s_tot[tid];
+    __syncthreads();
+  }
+}
+
+// Rows are converted to fp16 with a power-of-two scale putting the row's max
+// magnitude in [2^14, 2^15) (exact for bf16 input; the same rule as the
+// prefill GEMM's activation preparation).
+template <typename XT>
+__global__ void __launch_bounds__(256) k_moe_gather_prep(const XT* __restrict__ x, const int* __restrict__ sorted_tok,
+                                                         int P, int H, __half* __restrict__ a16,
+                                                         float* __restrict__ ascale) {
+  const int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (p >= P) return;
+  const XT* xr = x + (int64_t)sorted_tok[p] * H;
+  float amax = 0.f;
+  for (int i = lane; i < H; i += 32) amax = fmaxf(amax, fabsf(to_f32(xr[i])));
+#pragma unroll
+  for (int s = 16; s > 0; s >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, s));
+  int sh = 0;
+  if (amax > 0.f && amax < INFINITY) {
+    int e;
+    frexpf(amax, &e);
+    sh = (e - 1) - 14;
+  }
+  const float inv = ldexpf(1.0f, -sh);
+  __half* o = a16 + (int64_t)p * H;
+  for (int i = lane; i < H; i += 32) o[i] = __float2half_rn(to_f32(xr[i]) * inv);
+  if (lane == 0) ascale[p] = ldexpf(1.0f, sh);
+}
+
+// silu(g) * u (primitives.py:37-44: x / (1 + exp(-x)) times up), then the
+// fp16 row preparation of the down projection's activation.
+__global__ void __launch_bounds__(256) k_swiglu_prep(const float* __restrict__ g, const float* __restrict__ u, int P,
+                                                     int F, __half* __restrict__ h16, float* __restrict__ hscale) {
+  const int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (p >= P) return;
+  const float* gr = g + (int64_t)p * F;
+  const float* ur = u + (int64_t)p * F;
+  float amax = 0.f;
+  for (int i = lane; i < F; i += 32) {
+    const float gv = gr[i];
+    amax = fmaxf(amax, fabsf(gv / (1.0f + expf(-gv)) * ur[i]));
+  }
+#pragma unroll
+  for (int s = 16; s > 0; s >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, s));
+  int sh = 0;
+  if (amax > 0.f && amax < INFINITY) {
+    int e;
+    frexpf(amax, &e);
+    sh = (e - 1) - 14;
+  }
+  const float inv = ldexpf(1.0f, -sh);
+  __half* o = h16 + (int64_t)p * F;
+  for (int i = lane; i < F; i += 32) {
+    const float gv = gr[i];
+    o[i] = __float2half_rn(gv / (1.0f + expf(-gv)) * ur[i] * inv);
+  }
+  if (lane == 0) hscale[p] = ldexpf(1.0f, sh);
+}
+
+// out[t] = sum over the token's k expert rows, ascending expert order, of
+// row * weight: products rounded, then added, as the numpy accumulation does.
+__global__ void __launch_bounds__(256) k_moe_combine(const float* __restrict__ d, const int* __restrict__ topk_e,
+                                                     const float* __restrict__ topk_w, const int* __restrict__ pair_pos,
+                                                     int T, int H, int k, float* __restrict__ out) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (t >= T) return;
+  int ord[kMaxExperts];
+  for (int j = 0; j < k; ++j) ord[j] = j;
+  for (int a = 1; a < k; ++a) {            // insertion sort of the k slots by expert id
+    const int v = ord[a];
+    int b = a - 1;
+    while (b >= 0 && topk_e[(int64_t)t * k + ord[b]] > topk_e[(int64_t)t * k + v]) {
+      ord[b + 1] = ord[b];
+      --b;
+    }
+    ord[b + 1] = v;
+  }
+  for (int h = lane; h < H; h += 32) {
+    float acc = 0.f;
+    for (int j = 0; j < k; ++j) {
+      const int slot = (int)((int64_t)t * k + ord[j]);
+      acc = __fadd_rn(acc, __fmul_rn(d[(int64_t)pair_pos[slot] * H + h], topk_w[slot]));
+    }
+    out[(int64_t)t * H + h] = acc;
+  }
+}
+
+struct MoeWs {
+  int *topk_e, *sorted_tok, *pair_pos, *cnt, *off;
+  float *topk_w, *sorted_w, *ascale, *hscale, *g, *u, *d;
+  __half *a16, *h16;
+  int64_t bytes;
+};
+
+int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
+
+MoeWs carve(uint8_t* base, int64_t T, int64_t H, int64_t F, int E, int k) {
+  MoeWs w{};
+  const int64_t P = T * k;
+  int64_t o = 0;
+  auto take = [&](int64_t bytes) { uint8_t* p = base ? base + o : nullptr; o += align256(bytes); return p; };
+  w.topk_e = (int*)take(P * 4);
+  w.topk_w = (float*)take(P * 4);
+  w.sorted_tok = (int*)take(P * 4);
+  w.sorted_w = (float*)take(P * 4);
+  w.pair_pos = (int*)take(P * 4);
+  w.cnt = (int*)take(E * 4);
+  w.off = (int*)take(E * 4);
+  w.a16 = (__half*)take(P * H * 2);
+  w.ascale = (float*)take(P * 4);
+  w.g = (float*)take(P * F * 4);
+  w.u = (float*)take(P * F * 4);
+  w.h16 = (__half*)take(P * F * 2);
+  w.hscale = (float*)take(P * 4);
+  w.d = (float*)take(P * H * 4);
+  w.bytes = o;
+  return w;
+}
+
+}  // namespace
+
+extern "C" int64_t xm_moe_workspace_size(int64_t T, int64_t H, int64_t F, int E, int k) {
+  if (T < 1 || H < 1 || F < 1 || E < 1 || k < 1 || k > E) return 0;
+  return carve(nullptr, T, H, F, E, k).bytes;
+}
+
+extern "C" int xm_moe_forward(const void* d_x, int x_dtype, int64_t T, int64_t H, const float* d_gate, int E, int k,
+                              int64_t F, const void* const* h_w1, const void* const* h_w3, const void* const* h_w2,
+                              int qtype, float* d_out, void* d_ws, int64_t ws_bytes, void* stream) {
+  if (qtype != T_Q4_K) return xm_set_error(XM_ERR_UNSUPPORTED, "moe: expert type id %d has no tensor-core path", qtype);
+  if (E < 1 || E > kMaxExperts) return xm_set_error(XM_ERR_INVALID, "moe: %d experts (1..%d supported)", E, kMaxExperts);
+  if (k < 1 || k > E) return xm_set_error(XM_ERR_INVALID, "moe: num_experts_per_tok=%d outside 1..%d", k, E);
+  if (T < 1 || H < 256 || H % 256 || F < 256 || F % 256)
+    return xm_set_error(XM_ERR_INVALID, "moe: hidden and intermediate sizes must be positive multiples of 256");
+  if (T * k > (1 << 30)) return xm_set_error(XM_ERR_INVALID, "moe: too many tokens");
+  if (x_dtype != XM_DT_F32 && x_dtype != XM_DT_BF16 && x_dtype != XM_DT_F16)
+    return xm_set_error(XM_ERR_INVALID, "moe: bad x dtype %d", x_dtype);
+  if (!d_x || !d_gate || !d_out || !d_ws || !h_w1 || !h_w2 || !h_w3)
+    return xm_set_error(XM_ERR_INVALID, "moe: null pointer");
+  if (((uintptr_t)d_ws & 255) || ws_bytes < xm_moe_workspace_size(T, H, F, E, k))
+    return xm_set_error(XM_ERR_INVALID, "moe: workspace too small or not 256-byte aligned");
+  for (int e = 0; e < E; ++e)
+    if (!h_w1[e] || !h_w2[e] || !h_w3[e] || ((uintptr_t)h_w1[e] & 15) || ((uintptr_t)h_w2[e] & 15) ||
+        ((uintptr_t)h_w3[e] & 15))
+      return xm_set_error(XM_ERR_INVALID, "moe: expert %d weight pointer null or not 16-byte aligned", e);
+  cudaStream_t st = (cudaStream_t)stream;
+  MoeWs w = carve((uint8_t*)d_ws, T, H, F, E, k);
+  const int64_t P = T * k;
+
+  // expert weight pointers (host array of device pointers, passed to the kernels by value)
+  const uint8_t* tab[3 * kMaxExperts];
+  for (int e = 0; e < E; ++e) {
+    tab[e] = (const uint8_t*)h_w1[e];
+    tab[E + e] = (const uint8_t*)h_w3[e];
+    tab[2 * E + e] = (const uint8_t*)h_w2[e];
+  }
+
+  const unsigned tgrid = (unsigned)((T * 32 + 255) / 256);
+  if (x_dtype == XM_DT_F32)
+    k_moe_router<float><<<tgrid, 256, 0, st>>>((const float*)d_x, d_gate, (int)T, (int)H, E, k, w.topk_e, w.topk_w);
+  else if (x_dtype == XM_DT_BF16)
+    k_moe_router<__nv_bfloat16><<<tgrid, 256, 0, st>>>((const __nv_bfloat16*)d_x, d_gate, (int)T, (int)H, E, k,
+                                                         w.topk_e, w.topk_w);
+  else
+    k_moe_router<__half><<<tgrid, 256, 0, st>>>((const __half*)d_x, d_gate, (int)T, (int)H, E, k, w.topk_e, w.topk_w);
+  int rc = xm_check_launch("moe router");
+  if (rc) return rc;
+  k_moe_sort<<<1, 1024, 0, st>>>(w.topk_e, w.topk_w, (int)P, k, E, w.sorted_tok, w.sorted_w, w.pair_pos, w.cnt, w.off);
+  if ((rc = xm_check_launch("moe sort"))) return rc;
+  const unsigned pgrid = (unsigned)((P * 32 + 255) / 256);
+  if (x_dtype == XM_DT_F32)
+    k_moe_gather_prep<float><<<pgrid, 256, 0, st>>>((const float*)d_x, w.sorted_tok, (int)P, (int)H, w.a16, w.ascale);
+  else if (x_dtype == XM_DT_BF16)
+    k_moe_gather_prep<__nv_bfloat16><<<pgrid, 256, 0, st>>>((const __nv_bfloat16*)d_x, w.sorted_tok, (int)P, (int)H,
+                                                              w.a16, w.ascale);
+  else
+    k_moe_gather_prep<__half><<<pgrid, 256, 0, st>>>((const __half*)d_x, w.sorted_tok, (int)P, (int)H, w.a16, w.ascale);
+  if ((rc = xm_check_launch("moe gather"))) return rc;
+
+  const int64_t expect = std::max<int64_t>(1, P / E);
+  if ((rc = qgemm_q4k_grouped(w.a16, w.ascale, P, H, F, tab, w.cnt, w.off, E, T, expect, w.g, st))) return rc;
+  if ((rc = qgemm_q4k_grouped(w.a16, w.ascale, P, H, F, tab + E, w.cnt, w.off, E, T, expect, w.u, st))) return rc;
+  k_swiglu_prep<<<pgrid, 256, 0, st>>>(w.g, w.u, (int)P, (int)F, w.h16, w.hscale);
+  if ((rc = xm_check_launch("moe swiglu"))) return rc;
+  if ((rc = qgemm_q4k_grouped(w.h16, w.hscale, P, F, H, tab + 2 * E, w.cnt, w.off, E, T, expect, w.d, st))) return rc;
+  k_moe_combine<<<tgrid, 256, 0, st>>>(w.d, w.topk_e, w.topk_w, w.pair_pos, (int)T, (int)H, k, d_out);
+  return xm_check_launch("moe combine");
+}

@@ -31,6 +31,7 @@
 #include <algorithm>
 #include <mutex>
 
+#include "xm_internal.h"
 #include "xm_qtypes.cuh"
 
 namespace {
@@ -153,6 +154,18 @@ __global__ void __launch_bounds__(256) k_prep_rows(const XT* __restrict__ x, int
 // ---------------------------------------------------------------------------
 // The GEMM kernel.
 // ---------------------------------------------------------------------------
+// Grouped mode (MoE experts): group g = blockIdx.z multiplies rows
+// [off[g], off[g] + cnt[g]) of the activation with weight w[g]; the row
+// ranges come from the device-side expert sort, so they are read after the
+// grid dependency resolves and CTAs past the end of their group exit at once.
+constexpr int kMaxGroups = 32;
+struct GemmGroups {
+  int n;                               // 0: single GEMM
+  const int* cnt;
+  const int* off;
+  const uint8_t* w[kMaxGroups];        // passed by value: no device-side pointer table to build
+};
+
 struct GemmSmem {
   uint64_t full[kMaxStages], ab_empty[kMaxStages];   // full: A bytes + one arrival per decode warp
   uint64_t acc_full;
@@ -213,9 +226,9 @@ XM_DEV void decode_item(const RawItem& it, int h, int j, uint8_t* row, int n) {
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    k_qgemm_q4k_tc(const __grid_constant__ CUtensorMap map_a, const uint8_t* __restrict__ W, int M, int N,
+    k_qgemm_q4k_tc(const __grid_constant__ CUtensorMap map_a, const uint8_t* __restrict__ W0, int M, int N,
                    int K, int MT, int BN, int kStages, const float* __restrict__ rowscale,
-                   const float* __restrict__ bias, float* __restrict__ y) {
+                   const float* __restrict__ bias, float* __restrict__ y, GemmGroups groups) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte aligned carve-up: A stages | B stages | control
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -228,7 +241,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n0 = blockIdx.x * BN;
-  const int m0 = blockIdx.y * (MT * 128);
+  int mlo = 0, mhi = M;
+  const uint8_t* W = W0;
+  if (groups.n) {
+    grid_dep_wait();                   // counts and offsets come from the preceding sort kernel
+    const int g = blockIdx.z;
+    mlo = groups.off[g];
+    mhi = mlo + groups.cnt[g];
+    W = groups.w[g];
+  }
+  const int m0 = mlo + blockIdx.y * (MT * 128);
+  if (m0 >= mhi) return;               // whole CTA: nothing of this group left
   const int nkt = K / kBK;
 
   if (tid == 0) {
@@ -335,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t v[32];
         tmem_ld32(tmem + ((uint32_t)(sp * 32) << 16) + (uint32_t)(mt * BN + ch * 32), v);
         tmem_ld_wait();
-        const float rs = (mrow0 + lane) < M ? rowscale[mrow0 + lane] : 0.f;
+        const float rs = (mrow0 + lane) < mhi ? rowscale[mrow0 + lane] : 0.f;
 #pragma unroll
         for (int t = 0; t < 32; ++t) tile[lane * 33 + t] = __uint_as_float(v[t]) * rs;
         __syncwarp();
@@ -343,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float bv = (bias && nn < N) ? bias[nn] : 0.f;
         for (int r = 0; r < 32; ++r) {
           const int m = mrow0 + r;
-          if (m < M && nn < N) y[(int64_t)m * N + nn] = tile[r * 33 + lane] + bv;
+          if (m < mhi && nn < N) y[(int64_t)m * N + nn] = tile[r * 33 + lane] + bv;
         }
         __syncwarp();
       }
@@ -410,6 +433,64 @@ TileCfg choose_tile(int64_t M, int64_t N, int64_t K, int sms) {
 
 }  // namespace
 
+namespace {
+int encode_a16(CUtensorMap* map, const __half* a16, int64_t rows, int64_t k) {
+  EncodeTiledFn encode = get_encode();
+  if (!encode) return xm_set_error(XM_ERR_CUDA, "qgemm: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)k * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kBK, 128};
+  const cuuint32_t es[2] = {1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(a16), dims, strides, box, es,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return xm_set_error(XM_ERR_CUDA, "qgemm: activation tensor map (%d)", (int)r);
+  return XM_OK;
+}
+
+int launch_gemm(const CUtensorMap& map_a, const uint8_t* w, int64_t m, int64_t n, int64_t k, TileCfg cfg,
+                dim3 grid, const float* rowscale, const float* bias, float* y, const GemmGroups& groups,
+                cudaStream_t st) {
+  const int smem = 1024 + cfg.stages * (cfg.MT * kATileBytes + cfg.BN * kBK * 2) + (int)sizeof(GemmSmem);
+  cudaError_t e = cudaFuncSetAttribute(k_qgemm_q4k_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemm: smem attribute: %s", cudaGetErrorString(e));
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = grid;
+  lc.blockDim = dim3(kThreads);
+  lc.dynamicSmemBytes = smem;
+  lc.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  e = cudaLaunchKernelEx(&lc, k_qgemm_q4k_tc, map_a, w, (int)m, (int)n, (int)k, cfg.MT, cfg.BN, cfg.stages, rowscale,
+                         bias, y, groups);
+  if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemm launch: %s", cudaGetErrorString(e));
+  return xm_check_launch("qgemm");
+}
+}  // namespace
+
+int qgemm_q4k_grouped(const __half* a16, const float* rowscale, int64_t P, int64_t K, int64_t N,
+                      const uint8_t* const* h_w, const int* d_cnt, const int* d_off, int G, int64_t max_rows,
+                      int64_t expect_rows, float* y, cudaStream_t st) {
+  if (K % 256 || K < 256 || N < 1 || P < 1 || G < 1 || G > kMaxGroups)
+    return xm_set_error(XM_ERR_INVALID, "grouped qgemm: bad shape");
+  GemmGroups groups{};
+  groups.n = G;
+  groups.cnt = d_cnt;
+  groups.off = d_off;
+  for (int g = 0; g < G; ++g) groups.w[g] = h_w[g];
+  CUtensorMap map_a;
+  int rc = encode_a16(&map_a, a16, P, K);
+  if (rc) return rc;
+  // tile shape for the expected rows per group, grid for the worst case
+  TileCfg cfg = choose_tile(expect_rows, N * G, K, sm_count_dev());
+  const dim3 grid((unsigned)((N + cfg.BN - 1) / cfg.BN), (unsigned)((max_rows + cfg.MT * 128 - 1) / (cfg.MT * 128)),
+                  (unsigned)G);
+  return launch_gemm(map_a, nullptr, P, N, K, cfg, grid, rowscale, nullptr, y, groups, st);
+}
+
 extern "C" int64_t xm_qgemm_workspace_size(int64_t m, int64_t k) {
   if (m <= 0 || k <= 0) return 0;
   return ((m * k * 2 + 255) / 256) * 256 + m * 4;
@@ -434,8 +515,6 @@ extern "C" int xm_qgemm(int qtype, const void* d_w, int64_t w_bytes, int64_t n, 
     return xm_set_error(XM_ERR_INVALID, "qgemm: weight/x must be 16-byte and workspace 256-byte aligned");
   if (workspace_bytes < xm_qgemm_workspace_size(m, k))
     return xm_set_error(XM_ERR_INVALID, "qgemm: workspace too small");
-  EncodeTiledFn encode = get_encode();
-  if (!encode) return xm_set_error(XM_ERR_CUDA, "qgemm: cuTensorMapEncodeTiled unavailable");
   cudaStream_t st = (cudaStream_t)stream;
 
   __half* x16 = (__half*)d_workspace;
@@ -452,33 +531,9 @@ extern "C" int xm_qgemm(int qtype, const void* d_w, int64_t w_bytes, int64_t n, 
 
   const TileCfg cfg = choose_tile(m, n, k, sm_count_dev());
   CUtensorMap map_a;
-  {
-    const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
-    const cuuint64_t strides[1] = {(cuuint64_t)k * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)kBK, 128};
-    const cuuint32_t es[2] = {1, 1};
-    CUresult r = encode(&map_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x16, dims, strides, box, es,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return xm_set_error(XM_ERR_CUDA, "qgemm: activation tensor map (%d)", (int)r);
-  }
-  const int smem = 1024 + cfg.stages * (cfg.MT * kATileBytes + cfg.BN * kBK * 2) + (int)sizeof(GemmSmem);
-  cudaError_t e = cudaFuncSetAttribute(k_qgemm_q4k_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemm: smem attribute: %s", cudaGetErrorString(e));
+  rc = encode_a16(&map_a, x16, m, k);
+  if (rc) return rc;
   const dim3 grid((unsigned)((n + cfg.BN - 1) / cfg.BN), (unsigned)((m + cfg.MT * 128 - 1) / (cfg.MT * 128)));
-  cudaLaunchConfig_t lc = {};
-  lc.gridDim = grid;
-  lc.blockDim = dim3(kThreads);
-  lc.dynamicSmemBytes = smem;
-  lc.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  lc.attrs = attr;
-  lc.numAttrs = 1;
-  e = cudaLaunchKernelEx(&lc, k_qgemm_q4k_tc, map_a, (const uint8_t*)d_w, (int)m, (int)n, (int)k, cfg.MT, cfg.BN,
-                         cfg.stages,
-                         (const float*)rowscale, d_bias, d_y);
-  if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemm launch: %s", cudaGetErrorString(e));
-  return xm_check_launch("qgemm");
+  return launch_gemm(map_a, (const uint8_t*)d_w, m, n, k, cfg, grid, rowscale, d_bias, d_y,
+                     GemmGroups{}, st);
 }

@@ -1,0 +1,95 @@
+"""GPU drop-in for the reference's ``MoELayer`` (moe.py:7-119) on quantized experts.
+
+``MoELayer(config, weights)(x)`` takes the reference's config keys
+(``num_experts``, ``num_experts_per_tok``, ``hidden_act``) and its nested
+weight dict (``weights["gate"]["weight"]`` -- fp32 router, (E, H) --
+and ``weights["experts"][str(i)]["w1" | "w2" | "w3"]["weight"]``), with the
+expert weights given as :class:`~xanosmerks_b200.ops.GGUFTensor` (blocks
+resident on the GPU).  The same argument checks and exceptions as the
+reference are raised.  The forward pass runs entirely on the GPU
+(``xm_moe_forward``): routing, stable sort by expert, grouped tensor-core
+GEMMs, SwiGLU and the ordered combine.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from ._lib import DT_BF16, DT_F16, DT_F32, check, lib
+from .ops import GGUFTensor, _back, _to_device_x, _workspace
+
+_DT = {torch.float32: DT_F32, torch.bfloat16: DT_BF16, torch.float16: DT_F16}
+
+
+class MoELayer:
+    """Sparse (top-k) or dense (k == E) mixture of SwiGLU experts."""
+
+    def __init__(self, config, weights):
+        self.num_experts = config["num_experts"]
+        self.num_experts_per_tok = config["num_experts_per_tok"]
+        self.activation = config.get("hidden_act", "silu")
+        if self.num_experts_per_tok < 1:
+            raise ValueError(f"MoELayer: num_experts_per_tok={self.num_experts_per_tok} < 1")
+        if self.num_experts_per_tok > self.num_experts:
+            raise ValueError(f"MoELayer: num_experts_per_tok={self.num_experts_per_tok} "
+                             f"> num_experts={self.num_experts}")
+        if self.activation not in ("silu", "swish"):
+            raise NotImplementedError(f"MoELayer on the GPU supports silu experts, not {self.activation}")
+        gate_w = weights["gate"]["weight"]
+        gate_w = gate_w if isinstance(gate_w, torch.Tensor) else torch.as_tensor(np.asarray(gate_w, np.float32))
+        if gate_w.ndim != 2:
+            raise ValueError(f"MoELayer: gate.weight must be 2-D, got {gate_w.ndim}-D")
+        self.w1, self.w2, self.w3 = [], [], []
+        for i in range(self.num_experts):
+            exp = weights["experts"][str(i)]
+            for name, dst in (("w1", self.w1), ("w2", self.w2), ("w3", self.w3)):
+                w = exp[name]["weight"]
+                if not isinstance(w, GGUFTensor):
+                    raise TypeError("expert weights must be GGUFTensor (quantized blocks resident on the GPU)")
+                dst.append(w)
+        self.device = self.w1[0].device
+        self.gate = gate_w.to(device=self.device, dtype=torch.float32).contiguous()
+        self.hidden = self.gate.shape[1]
+        self.intermediate = self.w1[0].shape[0]
+        qt = {w.qtype.type_id for w in self.w1 + self.w2 + self.w3}
+        if len(qt) != 1:
+            raise NotImplementedError("all expert weights must share one block type")
+        self.qtype = qt.pop()
+        E = self.num_experts
+        self._p1 = (ctypes.c_void_p * E)(*[w.data.data_ptr() for w in self.w1])
+        self._p3 = (ctypes.c_void_p * E)(*[w.data.data_ptr() for w in self.w3])
+        self._p2 = (ctypes.c_void_p * E)(*[w.data.data_ptr() for w in self.w2])
+        self._is_dense = self.num_experts_per_tok == self.num_experts
+
+    def forward_device(self, x: torch.Tensor) -> torch.Tensor:
+        """x: CUDA tensor (..., H) -> fp32 CUDA tensor of the same shape."""
+        H, F, E, k = self.hidden, self.intermediate, self.num_experts, self.num_experts_per_tok
+        if x.shape[-1] != H:
+            raise ValueError(f"x has {x.shape[-1]} features, the router expects {H}")
+        if x.dtype not in _DT:
+            x = x.float()
+        xf = x.reshape(-1, H).contiguous()
+        T = xf.shape[0]
+        out = torch.empty((T, H), dtype=torch.float32, device=x.device)
+        wsz = lib.xm_moe_workspace_size(T, H, F, E, k)
+        ws = _workspace(x.device, wsz)
+        with torch.cuda.device(x.device):
+            check(lib.xm_moe_forward(xf.data_ptr(), _DT[xf.dtype], T, H, self.gate.data_ptr(), E, k, F,
+                                     self._p1, self._p3, self._p2, self.qtype, out.data_ptr(), ws.data_ptr(),
+                                     ws.numel(), torch.cuda.current_stream(x.device).cuda_stream), "moe")
+        return out.reshape(x.shape)
+
+    def __call__(self, x):
+        """x: (batch, seq, hidden) -> (batch, seq, hidden), as moe.py:54-115."""
+        xd, how = _to_device_x(x, self.device)
+        return _back(self.forward_device(xd), how)
+
+    def __repr__(self):
+        mode = "dense" if self._is_dense else f"top-{self.num_experts_per_tok}"
+        return f"<MoELayer experts={self.num_experts} {mode} activation={self.activation}>"
+
+
+__all__ = ["MoELayer"]
