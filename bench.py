@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the prefill (tensor-core GEMM) sweep")
+    ap.add_argument("--moe", action="store_true",
+                    help="only time the Mixtral-shape MoE block (8 experts, top-2, 1024 tokens, 4096 -> 14336)")
     ap.add_argument("--gemm-m", type=int, default=0,
                     help="only time the prefill GEMM with this many activation rows (profiling mode)")
     return ap.parse_args()
@@ -388,8 +390,51 @@ def run_gemm_only(args):
                       "TFLOPS": round(2.0 * mm * N * K / us / 1e6, 1), "clocks": clk.summary()}), flush=True)
 
 
+def moe_case(dev, T=1024, E=8, k=2, H=4096, F=14336, seed=0):
+    """Mixtral-shape MoE block with random-init Q4_K experts (seeded)."""
+    import torch
+    from xanosmerks_b200.moe import MoELayer
+    from xanosmerks_b200.ops import GGUFTensor
+    from xanosmerks_b200.synth import make_weight
+    rng = np.random.default_rng(seed)
+    gate = rng.standard_normal((E, H)).astype(np.float32) * 0.02
+    weights = {"gate": {"weight": gate}, "experts": {}}
+    for e in range(E):
+        weights["experts"][str(e)] = {
+            wn: {"weight": GGUFTensor(make_weight("Q4_K", *shape, seed=seed * 1000 + 3 * e + i), "Q4_K", shape,
+                                      device=dev)}
+            for i, (wn, shape) in enumerate((("w1", (F, H)), ("w3", (F, H)), ("w2", (H, F))))}
+    layer = MoELayer({"num_experts": E, "num_experts_per_tok": k, "hidden_act": "silu"}, weights)
+    x = torch.from_numpy(rng.standard_normal((1, T, H)).astype(np.float32)).to(dev).to(torch.bfloat16)
+    flops = 2.0 * T * k * 3 * F * H
+    return layer, x, flops
+
+
+def run_moe_only(args):
+    import torch
+    dev = torch.device("cuda", 0)
+    layer, x, flops = moe_case(dev)
+    for _ in range(args.warmup):
+        layer.forward_device(x)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(0) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            layer.forward_device(x)
+        e1.record()
+        torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    print(json.dumps({"moe": "Mixtral-shape block, 8 experts top-2, 1024 tokens, 4096->14336 Q4_K",
+                      "us": round(us, 1), "TFLOPS": round(flops / us / 1e6, 1),
+                      "tokens_per_s": round(1024 / us * 1e6, 1), "clocks": clk.summary()}), flush=True)
+
+
 def main():
     args = parse()
+    if args.moe:
+        run_moe_only(args)
+        return
     if args.gemm_m:
         run_gemm_only(args)
         return
