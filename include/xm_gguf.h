@@ -40,6 +40,11 @@ extern "C" {
 #define XM_DT_F16 1
 #define XM_DT_BF16 2
 
+/* activation prologues of xm_qgemv_ex */
+#define XM_PRO_NONE 0    /* v = x */
+#define XM_PRO_RMSNORM 1 /* v = (x / sqrt(mean(x^2) + eps)) * norm_w */
+#define XM_PRO_SWIGLU 2  /* v = silu(x[:, :k]) * x[:, k:2k]  (x rows hold 2k values) */
+
 /* ABI version of this header (bumped on any signature change). */
 int xm_abi_version(void);
 
@@ -103,6 +108,27 @@ int xm_qgemv_presplit(int qtype, const void* d_w, int64_t w_bytes, int64_t n, in
                       int64_t m, const void* d_workspace, int64_t workspace_bytes,
                       const float* d_bias, float* d_y, void* stream);
 
+/*
+ * xm_qgemv with the decoder's neighbours fused in:
+ *   y[m][n] (+)= sum_k pro(x)[m][k] * W[n][k] (+ bias[n])
+ * `prologue` transforms each activation row before the product (XM_PRO_*:
+ * RMSNorm with weight d_norm_w [k] and eps, or SwiGLU of a row holding gate
+ * then up, 2k values); `x_stride` is the row pitch of x in elements (>= k, or
+ * >= 2k for SwiGLU).  With `accumulate` the product is added to y instead of
+ * overwriting it (the residual add).  Block types with an integer-dot path
+ * (Q4_K, Q5_K, Q6_K, Q8_0) take any prologue; others only XM_PRO_NONE without
+ * accumulate.  Workspace as for xm_qgemv (NULL allowed only where no split is
+ * needed: Q4_K, m = 1, k = 4096 without SwiGLU).
+ *
+ * Replaces FusedRMSNormLinearOp.forward (ops.py:107-123), the MLP's
+ * `swiglu(gate, up) @ W_down.T` (forward.py:97-101) and the residual adds
+ * `x = residual + h` around them (forward.py:111, :116).
+ */
+int xm_qgemv_ex(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k,
+                const void* d_x, int x_dtype, int64_t m, int64_t x_stride, int prologue,
+                const float* d_norm_w, float eps, const float* d_bias, float* d_y, int accumulate,
+                void* d_workspace, int64_t workspace_bytes, void* stream);
+
 /* The exact path of xm_qgemv alone (every weight rounded to the reference's
  * fp16 value, fp32 products); the cross-check of the integer-dot path. */
 int xm_qgemv_exact(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k,
@@ -164,6 +190,44 @@ int xm_moe_forward(const void* d_x, int x_dtype, int64_t T, int64_t H, const flo
 int xm_qgemv_noalloc(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k,
                      const void* d_x, int x_dtype, int64_t m, const float* d_bias, float* d_y,
                      void* stream);
+
+/*
+ * Decoder-step kernels around the projections (Llama-style layer).  Head dim
+ * 128 only; the caches are fp16 [B][Hk][max_ctx][128].  All of these launch
+ * with programmatic dependent launch and run without host synchronisation.
+ *
+ * xm_embed: out[b][:] = fp16-rounded dequantized row ids[b] of a GGUF table
+ * (vocab rows of D) -- the reference indexes its dequantized embedding
+ * (forward.py:151).
+ *
+ * xm_rope_append: for T tokens (token t of sequence seq[t] at position
+ * pos[t]), qkv row t = [q | k | v] (Hq, Hk, Hk heads, fp32, row pitch
+ * qkv_stride): rotate-half rotary embedding of q and k in place (angle
+ * pos / theta^(2i/128)), and k, v appended to the caches at that position
+ * (attention.py:66-70, KV append of attention.py:99-104).
+ *
+ * xm_attention: causal GQA attention of Lq (<= 8) new tokens per sequence
+ * (tokens b*Lq + j of qkv; token j of sequence b sees keys 0 .. pos0[b] + j)
+ * over the caches, out row b*Lq + j = softmax(q k^T / sqrt(128)) v per query
+ * head (Hq / Hk <= 8 query heads share a KV head); attention.py:105-115 with
+ * ninewas9's scaled_dot_product_attention.  Keys are split 64 per CTA; the
+ * partial softmaxes meet in `d_workspace` (xm_attention_workspace_size bytes,
+ * zeroed once before the first call; every call leaves it ready for the next).
+ *
+ * xm_argmax: out[b] = first index of the maximum of logits row b (greedy
+ * sampling, sampling.py:51-52 `sample_greedy`).
+ *
+ * These entry points have no C counterpart in the reference (it is numpy).
+ */
+int xm_embed(int qtype, const void* d_table, int64_t table_bytes, int64_t vocab, int64_t D, const int* d_ids,
+             int64_t B, float* d_out, void* stream);
+int xm_rope_append(float* d_qkv, int64_t qkv_stride, const int* d_seq, const int* d_pos, int64_t T, int Hq, int Hk,
+                   int head_dim, float theta, int64_t max_ctx, void* d_kcache, void* d_vcache, void* stream);
+int64_t xm_attention_workspace_size(int64_t B, int Hk, int64_t max_ctx);
+int xm_attention(const float* d_qkv, int64_t qkv_stride, const void* d_kcache, const void* d_vcache,
+                 const int* d_pos0, int64_t B, int Lq, int Hq, int Hk, int head_dim, int64_t max_ctx, float* d_out,
+                 int64_t out_stride, void* d_workspace, int64_t workspace_bytes, void* stream);
+int xm_argmax(const float* d_logits, int64_t B, int64_t V, int* d_out, void* stream);
 
 #ifdef __cplusplus
 }

@@ -62,5 +62,22 @@ def test_host_side_validation_without_launch():
     assert L.xm_qgemv(12, None, 0, 4, 200, None, 0, 1, None, None, None, 0, None) == _lib.XM_ERR_INVALID
     assert L.xm_qgemv(0, None, 0, 4, 256, None, 0, 1, None, None, None, 0, None) == _lib.XM_ERR_UNSUPPORTED
     assert L.xm_qgemv(12, None, 100, 4, 256, None, 0, 1, None, None, None, 0, None) == _lib.XM_ERR_INVALID
-    assert L.xm_qgemv_workspace_size(4096, 1) == 128 * 80
+    # a single row of 4096 also carries the lane-major copy of the split (9,216 B)
+    assert L.xm_qgemv_workspace_size(4096, 1) == 128 * 80 + 9216
+    assert L.xm_qgemv_workspace_size(4096, 2) == 2 * 128 * 80
+    # fused-prologue GEMV: unknown prologue, RMSNorm without weights, short row pitch
+    assert L.xm_qgemv_ex(14, None, 0, 4, 256, None, 0, 1, 256, 3, None, 1e-5, None, None, 0, None, 0,
+                         None) == _lib.XM_ERR_INVALID
+    assert L.xm_qgemv_ex(14, None, 0, 4, 256, None, 0, 1, 256, _lib.PRO_RMSNORM, None, 1e-5, None, None, 0, None,
+                         0, None) == _lib.XM_ERR_INVALID
+    assert L.xm_qgemv_ex(14, None, 0, 4, 256, None, 0, 1, 256, _lib.PRO_SWIGLU, None, 1e-5, None, None, 0, None,
+                         0, None) == _lib.XM_ERR_INVALID
+    # decoder kernels: head_dim other than 128 is unsupported, bad shapes are invalid
+    assert L.xm_rope_append(None, 0, None, None, 1, 32, 8, 64, 5e5, 16, None, None, None) == _lib.XM_ERR_UNSUPPORTED
+    assert L.xm_attention(None, 0, None, None, None, 1, 9, 32, 8, 128, 16, None, 0, None, 0,
+                          None) == _lib.XM_ERR_INVALID
+    assert L.xm_attention(None, 0, None, None, None, 1, 1, 32, 3, 128, 16, None, 0, None, 0,
+                          None) == _lib.XM_ERR_INVALID
+    assert L.xm_embed(0, None, 0, 10, 4096, None, 1, None, None) == _lib.XM_ERR_UNSUPPORTED
+    assert L.xm_argmax(None, 0, 10, None, None) == _lib.XM_ERR_INVALID
     assert L.xm_qgemv_workspace_size(100, 1) == 0

@@ -18,10 +18,12 @@ XM_ERR_UNSUPPORTED = -2
 XM_ERR_CUDA = -3
 
 DT_F32, DT_F16, DT_BF16 = 0, 1, 2
+PRO_NONE, PRO_RMSNORM, PRO_SWIGLU = 0, 1, 2
 
 _i64 = ctypes.c_int64
 _vp = ctypes.c_void_p
 _int = ctypes.c_int
+_f32 = ctypes.c_float
 
 # name -> (restype, argtypes); every symbol the header declares
 SIGNATURES = {
@@ -41,6 +43,14 @@ SIGNATURES = {
     "xm_moe_forward": (_int, [_vp, _int, _i64, _i64, _vp, _int, _int, _i64, ctypes.POINTER(_vp),
                               ctypes.POINTER(_vp), ctypes.POINTER(_vp), _int, _vp, _vp, _i64, _vp]),
     "xm_qgemv_noalloc": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _int, _i64, _vp, _vp, _vp]),
+    "xm_qgemv_ex": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _int, _i64, _i64, _int, _vp, _f32, _vp, _vp, _int,
+                           _vp, _i64, _vp]),
+    "xm_embed": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp]),
+    "xm_rope_append": (_int, [_vp, _i64, _vp, _vp, _i64, _int, _int, _int, _f32, _i64, _vp, _vp, _vp]),
+    "xm_attention_workspace_size": (_i64, [_i64, _int, _i64]),
+    "xm_attention": (_int, [_vp, _i64, _vp, _vp, _vp, _i64, _int, _int, _int, _int, _i64, _vp, _i64, _vp, _i64,
+                            _vp]),
+    "xm_argmax": (_int, [_vp, _i64, _i64, _vp, _vp]),
 }
 
 

@@ -13,3 +13,12 @@
 int qgemm_q4k_grouped(const __half* a16, const float* rowscale, int64_t P, int64_t K, int64_t N,
                       const uint8_t* const* h_w, const int* d_cnt, const int* d_off, int G, int64_t max_rows,
                       int64_t expect_rows, float* y, cudaStream_t st);
+
+// Generic integer-dot GEMV (Q4_K, Q5_K, Q6_K, Q8_0; k % 128 == 0, k <= 16384)
+// over a group-major activation split in d_ws; y (+)= W x (+ bias).
+bool gemv_kq_supported(int qtype, int64_t n, int64_t k, int64_t m);
+int gemv_kq(int qtype, const uint8_t* W, int64_t n, int64_t k, int64_t m, const void* d_ws, const float* bias,
+            float* y, int accumulate, cudaStream_t st);
+// Group-major activation split of m rows of k values with an XM_PRO_* prologue.
+int split_rows(const void* d_x, int x_dtype, int64_t m, int64_t k, int64_t x_stride, int prologue,
+               const float* norm_w, float eps, void* d_ws, cudaStream_t st);

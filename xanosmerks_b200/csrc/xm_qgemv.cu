@@ -19,7 +19,8 @@
 #include <mutex>
 #include <type_traits>
 
-#include "xm_qtypes.cuh"
+#include "xm_gemv_dot.cuh"
+#include "xm_internal.h"
 
 namespace {
 
@@ -40,40 +41,23 @@ constexpr int kLaneMajorBytes = 8192 + 1024;
 template <typename XT>
 __global__ void __launch_bounds__(kThreads) k_split_x(const XT* __restrict__ x, int64_t mg, int G,
                                                       int8_t* __restrict__ pieces, float4* __restrict__ ts,
-                                                      int lane_major) {
+                                                      int8_t* __restrict__ lane_major) {
   const int lane = threadIdx.x & 31;
   const int64_t grp = ((int64_t)blockIdx.x * kThreads + threadIdx.x) >> 5;
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (grp >= mg) return;
   const float v = to_f32(x[grp * 32 + lane]);
-  float amax = fabsf(v);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  // half sums in a fixed shuffle order (deterministic)
-  float s = v;
-#pragma unroll
-  for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  const float s_lo = __shfl_sync(0xffffffffu, s, 0), s_hi = __shfl_sync(0xffffffffu, s, 16);
-  int x0 = 0, x1 = 0;
-  float t = 0.f;
-  if (amax > 0.f) {
-    const float sc = amax / 127.0f;
-    const float u = v * (1.0f / sc);
-    const float r0 = rintf(u);
-    x0 = (int)r0;
-    x1 = (int)rintf((u - r0) * 254.0f);
-    x1 = max(-127, min(127, x1));
-    t = sc / 254.0f;
-  }
+  int x0, x1;
+  float t, s_lo, s_hi;
+  split_group(v, x0, x1, t, s_lo, s_hi);
+  pieces[grp * kPieceBytes + lane] = (int8_t)x0;
+  pieces[grp * kPieceBytes + 32 + lane] = (int8_t)x1;
+  if (lane == 0) ts[grp] = make_float4(t, s_lo, s_hi, s_lo + s_hi);
   if (lane_major) {
     const int L = (int)(grp >> 2), i = (int)(grp & 3);
-    pieces[((4 * i + (lane >> 4)) * 32 + L) * 16 + (lane & 15)] = (int8_t)x0;
-    pieces[((4 * i + 2 + (lane >> 4)) * 32 + L) * 16 + (lane & 15)] = (int8_t)x1;
-    if (lane == 0) reinterpret_cast<float2*>(pieces + 8192)[32 * i + L] = make_float2(t, s_lo + s_hi);
-  } else {
-    pieces[grp * kPieceBytes + lane] = (int8_t)x0;
-    pieces[grp * kPieceBytes + 32 + lane] = (int8_t)x1;
-    if (lane == 0) ts[grp] = make_float4(t, s_lo, s_hi, s_lo + s_hi);
+    lane_major[((4 * i + (lane >> 4)) * 32 + L) * 16 + (lane & 15)] = (int8_t)x0;
+    lane_major[((4 * i + 2 + (lane >> 4)) * 32 + L) * 16 + (lane & 15)] = (int8_t)x1;
+    if (lane == 0) reinterpret_cast<float2*>(lane_major + 8192)[32 * i + L] = make_float2(t, s_lo + s_hi);
   }
 }
 
@@ -85,6 +69,9 @@ XM_DEV uint4 ldg_v4(const void* p) {
 
 XM_DEV uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xFF; }
 
+// y = v, or y += v for the residual-add (accumulate) form
+XM_DEV void store_out(float* p, float v, int accumulate) { *p = accumulate ? *p + v : v; }
+
 // ---------------------------------------------------------------------------
 // Q4_K integer-dot GEMV.  A warp serves 4 rows; 8 lanes per row, lane cl
 // handles super-blocks c = cl, cl+8, ... of its row.  The 4 rows of a warp read
@@ -94,7 +81,8 @@ template <int M>
 __global__ void __launch_bounds__(kThreads) k_qgemv_q4k_dp4a(const uint8_t* __restrict__ W, int N, int nb,
                                                              const int8_t* __restrict__ pieces,
                                                              const float4* __restrict__ ts,
-                                                             const float* __restrict__ bias, float* __restrict__ y) {
+                                                             const float* __restrict__ bias, float* __restrict__ y,
+                                                             int accumulate) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int slot = lane >> 3, cl = lane & 7;
   const int G = nb * 8;  // 32-element groups per row
@@ -159,21 +147,12 @@ __global__ void __launch_bounds__(kThreads) k_qgemv_q4k_dp4a(const uint8_t* __re
       v += __shfl_xor_sync(0xffffffffu, v, 4);
       v += __shfl_xor_sync(0xffffffffu, v, 2);
       v += __shfl_xor_sync(0xffffffffu, v, 1);
-      if (cl == 0 && valid) y[(int64_t)m * N + row] = v + (bias ? bias[row] : 0.f);
+      if (cl == 0 && valid) store_out(&y[(int64_t)m * N + row], v + (bias ? bias[row] : 0.f), accumulate);
     }
   }
 }
 
-int sm_count() {
-  static int n = 0;
-  if (!n) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
-  }
-  return n;
-}
+int sm_count() { return xm_sm_count(); }
 
 // ---------------------------------------------------------------------------
 // Q4_K integer-dot GEMV, TMA-staged (the main decode kernel).
@@ -198,13 +177,6 @@ constexpr int kGemvStages = 2;
 constexpr int kSlotBytes = 32 * 144;
 constexpr int kColStride = 656;
 
-XM_DEV uint4 lds_v4(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
-XM_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-XM_DEV void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-// byte i of w as an exact float (magic-number conversion, no I2F)
-XM_DEV float byte_f(uint32_t w, int i) {
-  return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7650u | (uint32_t)i)) - 8388608.0f;
-}
 
 struct GemvSmem {
   int next_group;
@@ -217,7 +189,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_qgemv_q4k_tma(const uint8_t
                                                                    const int8_t* __restrict__ pieces,
                                                                    const float4* __restrict__ ts,
                                                                    const float* __restrict__ bias,
-                                                                   float* __restrict__ y) {
+                                                                   float* __restrict__ y, int accumulate) {
   constexpr int RW = 32 / LPR;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* slots = smem;                                                // [warps][stages][kSlotBytes]
@@ -351,7 +323,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_qgemv_q4k_tma(const uint8_t
         float v = acc[m];
 #pragma unroll
         for (int o = LPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (lc == 0 && r0 + lr < re) y[(int64_t)m * N + r0 + lr] = v + (bias ? bias[r0 + lr] : 0.f);
+        if (lc == 0 && r0 + lr < re)
+          store_out(&y[(int64_t)m * N + r0 + lr], v + (bias ? bias[r0 + lr] : 0.f), accumulate);
         acc[m] = 0.f;
       }
     }
@@ -391,13 +364,9 @@ constexpr int kWsSlotBytes = kWsRowsPerSlot * kRowBytes4096;
 constexpr int kWsCtlBytes = 256;
 static_assert((2 * kWsSlots + 1) * 8 + (kWsSlots + 1) * 4 <= kWsCtlBytes, "control block");
 static_assert((kWsSlots * kWsSlotBytes + kLaneMajorBytes + kWsCtlBytes) % 16 == 0, "x row alignment");
-constexpr int kWsSmem = kWsSlots * kWsSlotBytes + kLaneMajorBytes + kWsCtlBytes + 4096 * 4;
+// + 64 B behind the row of x for the RMSNorm partial sums
+constexpr int kWsSmem = kWsSlots * kWsSlotBytes + kLaneMajorBytes + kWsCtlBytes + 4096 * 4 + 64;
 
-XM_DEV int dp4a_us(uint32_t a, uint32_t b, int c) {   // unsigned bytes of a x signed bytes of b
-  int d;
-  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
 
 // Partial dot of one row's 128 weights (sub-block pairs 2h, 2h+1 of column c)
 // with this lane's digits: returns d*sum(sc*t*P) - dmin*sum(mn*sum_x).
@@ -439,14 +408,40 @@ XM_DEV float q4k_lane_dot(uint4 hd, uint4 q0, uint4 q1, uint4 q2, uint4 q3, int 
 // 4096).  Threads 0..255 work: thread t takes half (t&1) -- 16 elements -- of
 // 32-element group t>>1, so each thread writes whole 16-byte digit chunks and
 // the only cross-thread step is one shuffle for the group max and one for the
-// sum.  `x` is a shared-memory copy of the row.
+// sum.  `x` is a shared-memory copy of the row.  With norm_w the row is first
+// RMS-normalised, v = (x / sqrt(mean(x^2) + eps)) * norm_w (ops.py:115-117);
+// every consumer thread must then call this (it holds a consumer-only barrier).
 template <typename XT>
-XM_DEV void split_row4096_to_smem(const XT* x, uint8_t* xsm, int tid) {
-  if (tid >= 256) return;
+XM_DEV void split_row4096_to_smem(const XT* x, uint8_t* xsm, int tid, const float* norm_w, float eps, float* red) {
+  const bool work = tid < 256;
   const int g = tid >> 1, half = tid & 1;
   float v[16];
 #pragma unroll
-  for (int e = 0; e < 16; ++e) v[e] = to_f32(x[g * 32 + half * 16 + e]);
+  for (int e = 0; e < 16; ++e) v[e] = work ? to_f32(x[g * 32 + half * 16 + e]) : 0.f;
+  if (norm_w) {
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) ss = fmaf(v[e], v[e], ss);
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0 && work) red[tid >> 5] = ss;
+    asm volatile("bar.sync 1, %0;" ::"r"(kWsConsumers * 32) : "memory");
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) tot += red[w];
+    const float rms = sqrtf(tot / 4096.0f + eps);
+    if (work) {
+      const float4* nw = reinterpret_cast<const float4*>(norm_w + g * 32 + half * 16);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 w4 = nw[q];
+        v[4 * q] = (v[4 * q] / rms) * w4.x;
+        v[4 * q + 1] = (v[4 * q + 1] / rms) * w4.y;
+        v[4 * q + 2] = (v[4 * q + 2] / rms) * w4.z;
+        v[4 * q + 3] = (v[4 * q + 3] / rms) * w4.w;
+      }
+    }
+  }
+  if (!work) return;
   float amax = 0.f, s = 0.f;
 #pragma unroll
   for (int e = 0; e < 16; ++e) {
@@ -482,8 +477,9 @@ XM_DEV void split_row4096_to_smem(const XT* x, uint8_t* xsm, int tid) {
 template <typename XT>
 __global__ void __launch_bounds__(kWsThreads, 1) k_qgemv_q4k_k4096_m1(const uint8_t* __restrict__ W, int N,
                                                                       const void* __restrict__ xin,
+                                                                      const float* __restrict__ norm_w, float eps,
                                                                       const float* __restrict__ bias,
-                                                                      float* __restrict__ y) {
+                                                                      float* __restrict__ y, int accumulate) {
   extern __shared__ __align__(128) uint8_t ws_smem[];
   uint8_t* slots = ws_smem;                                            // [kWsSlots][kWsSlotBytes]
   uint8_t* xsm = ws_smem + kWsSlots * kWsSlotBytes;                    // lane-major digits
@@ -545,7 +541,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_qgemv_q4k_k4096_m1(const uint
       bulk_g2s(xrow, xin, 4096 * sizeof(XT), xbar);
     }
     mbar_wait_bounded(xbar, 0);
-    split_row4096_to_smem<XT>(xrow, xsm, tid);
+    split_row4096_to_smem<XT>(xrow, xsm, tid, norm_w, eps, reinterpret_cast<float*>(xrow + 4096));
     asm volatile("bar.sync 1, %0;" ::"r"(kWsConsumers * 32) : "memory");   // consumer warps only
   }
   const int c = lane >> 1, h = lane & 1;
@@ -591,14 +587,14 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_qgemv_q4k_k4096_m1(const uint
     float v = __shfl_xor_sync(0xffffffffu, upper ? v0 : v1, 16) + (upper ? v1 : v0);
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0) y[rb + r] = v + (bias ? bias[rb + r] : 0.f);
-    if (lane == 16 && two) y[rb + r + 1] = v + (bias ? bias[rb + r + 1] : 0.f);
+    if (lane == 0) store_out(&y[rb + r], v + (bias ? bias[rb + r] : 0.f), accumulate);
+    if (lane == 16 && two) store_out(&y[rb + r + 1], v + (bias ? bias[rb + r + 1] : 0.f), accumulate);
   }
 }
 
 template <typename XT>
-int launch_q4k_k4096_m1(const uint8_t* W, int64_t N, const void* xin, const float* bias, float* y,
-                        cudaStream_t st) {
+int launch_q4k_k4096_m1(const uint8_t* W, int64_t N, const void* xin, const float* norm_w, float eps,
+                        const float* bias, float* y, int accumulate, cudaStream_t st) {
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -619,7 +615,7 @@ int launch_q4k_k4096_m1(const uint8_t* W, int64_t N, const void* xin, const floa
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k_qgemv_q4k_k4096_m1<XT>, W, (int)N, xin, bias, y);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_qgemv_q4k_k4096_m1<XT>, W, (int)N, xin, norm_w, eps, bias, y, accumulate);
   if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemv launch: %s", cudaGetErrorString(e));
   return XM_OK;
 }
@@ -740,34 +736,48 @@ void launch_exact(int qtype, const uint8_t* W, int64_t N, int64_t K, const void*
 
 template <int M>
 void launch_q4k(const uint8_t* W, int64_t N, int64_t nb, const int8_t* pieces, const float4* ts, const float* bias,
-                float* y, cudaStream_t st) {
+                float* y, int accumulate, cudaStream_t st) {
   const int64_t warps = (N + 3) / 4;
   const unsigned grid = (unsigned)std::min<int64_t>((warps + 7) / 8, (int64_t)sm_count() * 4);
-  k_qgemv_q4k_dp4a<M><<<grid, kThreads, 0, st>>>(W, (int)N, (int)nb, pieces, ts, bias, y);
+  k_qgemv_q4k_dp4a<M><<<grid, kThreads, 0, st>>>(W, (int)N, (int)nb, pieces, ts, bias, y, accumulate);
 }
 
 }  // namespace
 
 // Workspace for the activation split: 64 B of digits + 16 B of (t, sums) per
-// 32-element group of x.
+// 32-element group of x (group-major), and for a single row of 4096 also the
+// lane-major copy that the K = 4096 Q4_K kernel reads (9,216 B behind it).
 extern "C" int64_t xm_qgemv_workspace_size(int64_t k, int64_t m) {
   if (k <= 0 || m <= 0 || (k % 32)) return 0;
-  return m * (k / 32) * (kPieceBytes + 16);
+  return m * (k / 32) * (kPieceBytes + 16) + (m == 1 && k == 4096 ? kLaneMajorBytes : 0);
 }
 
 namespace {
 
-bool integer_path_type(int qtype) { return qtype == T_Q4_K; }
+bool integer_path_type(int qtype) {
+  return qtype == T_Q4_K || qtype == T_Q5_K || qtype == T_Q6_K || qtype == T_Q8_0;
+}
 
-// The single-row K = 4096 kernel reads the lane-major layout; every other
+// The single-row K = 4096 Q4_K kernel reads the lane-major layout; every other
 // integer-path kernel reads the group-major one.
 bool lane_major_shape(int64_t m, int64_t k) { return m == 1 && k == 4096; }
 
+// Whether the integer path takes this type and shape (the Q4_K kernels take
+// any k % 256 == 0; the generic kernel has its own limits).
+bool integer_path(int qtype, int64_t n, int64_t k, int64_t m) {
+  if (qtype == T_Q4_K) return true;
+  return integer_path_type(qtype) && gemv_kq_supported(qtype, n, k, m);
+}
+
+int8_t* lane_major_part(const void* d_ws, int64_t m, int64_t k) {
+  return (int8_t*)d_ws + m * (k / 32) * (kPieceBytes + 16);
+}
+
 int split_activation(const void* d_x, int x_dtype, int64_t m, int64_t k, void* d_ws, cudaStream_t st) {
   const int G = (int)(k / 32);
-  const int lm = lane_major_shape(m, k) ? 1 : 0;
   int8_t* pieces = (int8_t*)d_ws;
   float4* ts = (float4*)((uint8_t*)d_ws + m * G * kPieceBytes);
+  int8_t* lm = lane_major_shape(m, k) ? lane_major_part(d_ws, m, k) : nullptr;
   const int64_t groups = m * G;
   const unsigned sgrid = (unsigned)((groups * 32 + kThreads - 1) / kThreads);
   if (x_dtype == XM_DT_F32)
@@ -792,7 +802,7 @@ int choose_lpr(int64_t nb) {
 
 template <int M, int LPR>
 int launch_q4k_tma_lpr(const uint8_t* W, int64_t N, int64_t nb, const int8_t* pieces, const float4* ts,
-                       const float* bias, float* y, cudaStream_t st) {
+                       const float* bias, float* y, int accumulate, cudaStream_t st) {
   const int smem = q4k_tma_smem(M, nb);
   static bool attr_set[64] = {};
   int dev = 0;
@@ -814,62 +824,68 @@ int launch_q4k_tma_lpr(const uint8_t* W, int64_t N, int64_t nb, const int8_t* pi
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k_qgemv_q4k_tma<M, LPR>, W, (int)N, (int)nb, pieces, ts, bias, y);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_qgemv_q4k_tma<M, LPR>, W, (int)N, (int)nb, pieces, ts, bias, y,
+                                     accumulate);
   if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemv launch: %s", cudaGetErrorString(e));
   return XM_OK;
 }
 
 template <int M>
 int launch_q4k_tma(const uint8_t* W, int64_t N, int64_t nb, const int8_t* pieces, const float4* ts, const float* bias,
-                   float* y, cudaStream_t st) {
+                   float* y, int accumulate, cudaStream_t st) {
   switch (choose_lpr(nb)) {
-    case 1: return launch_q4k_tma_lpr<M, 1>(W, N, nb, pieces, ts, bias, y, st);
-    case 2: return launch_q4k_tma_lpr<M, 2>(W, N, nb, pieces, ts, bias, y, st);
-    case 4: return launch_q4k_tma_lpr<M, 4>(W, N, nb, pieces, ts, bias, y, st);
-    case 8: return launch_q4k_tma_lpr<M, 8>(W, N, nb, pieces, ts, bias, y, st);
-    case 16: return launch_q4k_tma_lpr<M, 16>(W, N, nb, pieces, ts, bias, y, st);
-    default: return launch_q4k_tma_lpr<M, 32>(W, N, nb, pieces, ts, bias, y, st);
+    case 1: return launch_q4k_tma_lpr<M, 1>(W, N, nb, pieces, ts, bias, y, accumulate, st);
+    case 2: return launch_q4k_tma_lpr<M, 2>(W, N, nb, pieces, ts, bias, y, accumulate, st);
+    case 4: return launch_q4k_tma_lpr<M, 4>(W, N, nb, pieces, ts, bias, y, accumulate, st);
+    case 8: return launch_q4k_tma_lpr<M, 8>(W, N, nb, pieces, ts, bias, y, accumulate, st);
+    case 16: return launch_q4k_tma_lpr<M, 16>(W, N, nb, pieces, ts, bias, y, accumulate, st);
+    default: return launch_q4k_tma_lpr<M, 32>(W, N, nb, pieces, ts, bias, y, accumulate, st);
   }
 }
 
 constexpr int kMaxTmaSmem = 227 * 1024;
 
-int gemv_presplit(int qtype, const uint8_t* W, int64_t n, int64_t k, int64_t m, const void* d_ws,
-                  const float* bias, float* y, cudaStream_t st) {
+// GEMV from an activation split already in the workspace.  `lane_major`: the
+// workspace also holds the lane-major copy (split_activation writes it for a
+// single row of 4096).
+int gemv_presplit(int qtype, const uint8_t* W, int64_t n, int64_t k, int64_t m, const void* d_ws, bool lane_major,
+                  const float* bias, float* y, int accumulate, cudaStream_t st) {
+  if (qtype != T_Q4_K) return gemv_kq(qtype, W, n, k, m, d_ws, bias, y, accumulate, st);
   const int G = (int)(k / 32);
   const int8_t* pieces = (const int8_t*)d_ws;
   const float4* ts = (const float4*)((const uint8_t*)d_ws + m * G * kPieceBytes);
   const int64_t nb = k / 256;
-  (void)qtype;
-  if (lane_major_shape(m, k)) {
-    const int rc = launch_q4k_k4096_m1<void>(W, n, pieces, bias, y, st);
+  if (lane_major && lane_major_shape(m, k)) {
+    const int rc = launch_q4k_k4096_m1<void>(W, n, lane_major_part(d_ws, m, k), nullptr, 0.f, bias, y, accumulate,
+                                             st);
     if (rc) return rc;
     return xm_check_launch("qgemv(integer, k4096 m1)");
   }
   if (q4k_tma_smem(m, nb) <= kMaxTmaSmem) {
     int rc = XM_OK;
     switch (m) {
-      case 1: rc = launch_q4k_tma<1>(W, n, nb, pieces, ts, bias, y, st); break;
-      case 2: rc = launch_q4k_tma<2>(W, n, nb, pieces, ts, bias, y, st); break;
-      case 3: rc = launch_q4k_tma<3>(W, n, nb, pieces, ts, bias, y, st); break;
-      case 4: rc = launch_q4k_tma<4>(W, n, nb, pieces, ts, bias, y, st); break;
-      case 5: rc = launch_q4k_tma<5>(W, n, nb, pieces, ts, bias, y, st); break;
-      case 6: rc = launch_q4k_tma<6>(W, n, nb, pieces, ts, bias, y, st); break;
-      case 7: rc = launch_q4k_tma<7>(W, n, nb, pieces, ts, bias, y, st); break;
-      default: rc = launch_q4k_tma<8>(W, n, nb, pieces, ts, bias, y, st); break;
+      case 1: rc = launch_q4k_tma<1>(W, n, nb, pieces, ts, bias, y, accumulate, st); break;
+      case 2: rc = launch_q4k_tma<2>(W, n, nb, pieces, ts, bias, y, accumulate, st); break;
+      case 3: rc = launch_q4k_tma<3>(W, n, nb, pieces, ts, bias, y, accumulate, st); break;
+      case 4: rc = launch_q4k_tma<4>(W, n, nb, pieces, ts, bias, y, accumulate, st); break;
+      case 5: rc = launch_q4k_tma<5>(W, n, nb, pieces, ts, bias, y, accumulate, st); break;
+      case 6: rc = launch_q4k_tma<6>(W, n, nb, pieces, ts, bias, y, accumulate, st); break;
+      case 7: rc = launch_q4k_tma<7>(W, n, nb, pieces, ts, bias, y, accumulate, st); break;
+      default: rc = launch_q4k_tma<8>(W, n, nb, pieces, ts, bias, y, accumulate, st); break;
     }
     if (rc) return rc;
     return xm_check_launch("qgemv(integer, tma)");
   }
+  if (gemv_kq_supported(qtype, n, k, m)) return gemv_kq(qtype, W, n, k, m, d_ws, bias, y, accumulate, st);
   switch (m) {
-    case 1: launch_q4k<1>(W, n, nb, pieces, ts, bias, y, st); break;
-    case 2: launch_q4k<2>(W, n, nb, pieces, ts, bias, y, st); break;
-    case 3: launch_q4k<3>(W, n, nb, pieces, ts, bias, y, st); break;
-    case 4: launch_q4k<4>(W, n, nb, pieces, ts, bias, y, st); break;
-    case 5: launch_q4k<5>(W, n, nb, pieces, ts, bias, y, st); break;
-    case 6: launch_q4k<6>(W, n, nb, pieces, ts, bias, y, st); break;
-    case 7: launch_q4k<7>(W, n, nb, pieces, ts, bias, y, st); break;
-    default: launch_q4k<8>(W, n, nb, pieces, ts, bias, y, st); break;
+    case 1: launch_q4k<1>(W, n, nb, pieces, ts, bias, y, accumulate, st); break;
+    case 2: launch_q4k<2>(W, n, nb, pieces, ts, bias, y, accumulate, st); break;
+    case 3: launch_q4k<3>(W, n, nb, pieces, ts, bias, y, accumulate, st); break;
+    case 4: launch_q4k<4>(W, n, nb, pieces, ts, bias, y, accumulate, st); break;
+    case 5: launch_q4k<5>(W, n, nb, pieces, ts, bias, y, accumulate, st); break;
+    case 6: launch_q4k<6>(W, n, nb, pieces, ts, bias, y, accumulate, st); break;
+    case 7: launch_q4k<7>(W, n, nb, pieces, ts, bias, y, accumulate, st); break;
+    default: launch_q4k<8>(W, n, nb, pieces, ts, bias, y, accumulate, st); break;
   }
   return xm_check_launch("qgemv(integer)");
 }
@@ -893,6 +909,38 @@ int check_gemv_args(const char* who, int qtype, const void* d_w, int64_t w_bytes
   return XM_OK;
 }
 
+bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+int exact_path(int qtype, const uint8_t* W, int64_t n, int64_t k, const void* d_x, int x_dtype, int64_t m,
+               const float* bias, float* y, cudaStream_t st) {
+  switch (m) {
+    case 1: launch_exact<1>(qtype, W, n, k, d_x, x_dtype, bias, y, st); break;
+    case 2: launch_exact<2>(qtype, W, n, k, d_x, x_dtype, bias, y, st); break;
+    case 3: launch_exact<3>(qtype, W, n, k, d_x, x_dtype, bias, y, st); break;
+    case 4: launch_exact<4>(qtype, W, n, k, d_x, x_dtype, bias, y, st); break;
+    case 5: launch_exact<5>(qtype, W, n, k, d_x, x_dtype, bias, y, st); break;
+    case 6: launch_exact<6>(qtype, W, n, k, d_x, x_dtype, bias, y, st); break;
+    case 7: launch_exact<7>(qtype, W, n, k, d_x, x_dtype, bias, y, st); break;
+    default: launch_exact<8>(qtype, W, n, k, d_x, x_dtype, bias, y, st); break;
+  }
+  return xm_check_launch("qgemv(exact)");
+}
+
+template <typename XT>
+int launch_k4096_fused(const uint8_t* W, int64_t n, const void* x, const float* norm_w, float eps, const float* bias,
+                       float* y, int accumulate, cudaStream_t st) {
+  const int rc = launch_q4k_k4096_m1<XT>(W, n, x, norm_w, eps, bias, y, accumulate, st);
+  if (rc) return rc;
+  return xm_check_launch("qgemv(integer, k4096 m1, fused split)");
+}
+
+int k4096_fused(int x_dtype, const uint8_t* W, int64_t n, const void* x, const float* norm_w, float eps,
+                const float* bias, float* y, int accumulate, cudaStream_t st) {
+  if (x_dtype == XM_DT_F32) return launch_k4096_fused<float>(W, n, x, norm_w, eps, bias, y, accumulate, st);
+  if (x_dtype == XM_DT_BF16) return launch_k4096_fused<__nv_bfloat16>(W, n, x, norm_w, eps, bias, y, accumulate, st);
+  return launch_k4096_fused<__half>(W, n, x, norm_w, eps, bias, y, accumulate, st);
+}
+
 }  // namespace
 
 extern "C" int xm_split_activation(const void* d_x, int x_dtype, int64_t m, int64_t k, void* d_workspace,
@@ -902,7 +950,7 @@ extern "C" int xm_split_activation(const void* d_x, int x_dtype, int64_t m, int6
   if (x_dtype != XM_DT_F32 && x_dtype != XM_DT_BF16 && x_dtype != XM_DT_F16)
     return xm_set_error(XM_ERR_INVALID, "split_activation: bad x dtype %d", x_dtype);
   if (!d_x || !d_workspace) return xm_set_error(XM_ERR_INVALID, "split_activation: null pointer");
-  if (workspace_bytes < xm_qgemv_workspace_size(k, m) || ((uintptr_t)d_workspace & 15))
+  if (workspace_bytes < xm_qgemv_workspace_size(k, m) || !aligned16(d_workspace))
     return xm_set_error(XM_ERR_INVALID, "split_activation: workspace too small or not 16-byte aligned");
   return split_activation(d_x, x_dtype, m, k, d_workspace, (cudaStream_t)stream);
 }
@@ -913,14 +961,15 @@ extern "C" int xm_qgemv_presplit(int qtype, const void* d_w, int64_t w_bytes, in
   int64_t nb = 0;
   int rc = check_gemv_args("qgemv_presplit", qtype, d_w, w_bytes, n, k, m, &nb);
   if (rc) return rc;
-  if (!integer_path_type(qtype))
-    return xm_set_error(XM_ERR_UNSUPPORTED, "qgemv_presplit: type id %d has no integer-dot path", qtype);
-  if (((uintptr_t)d_w & 15) != 0) return xm_set_error(XM_ERR_INVALID, "qgemv_presplit: weight not 16-byte aligned");
-  if (!d_workspace || workspace_bytes < xm_qgemv_workspace_size(k, m) || ((uintptr_t)d_workspace & 15))
+  if (!integer_path(qtype, n, k, m))
+    return xm_set_error(XM_ERR_UNSUPPORTED, "qgemv_presplit: type id %d has no integer-dot path for this shape",
+                        qtype);
+  if (!aligned16(d_w)) return xm_set_error(XM_ERR_INVALID, "qgemv_presplit: weight not 16-byte aligned");
+  if (!d_workspace || workspace_bytes < xm_qgemv_workspace_size(k, m) || !aligned16(d_workspace))
     return xm_set_error(XM_ERR_INVALID, "qgemv_presplit: workspace too small or not 16-byte aligned");
   if (n == 0) return XM_OK;
   if (!d_y) return xm_set_error(XM_ERR_INVALID, "qgemv_presplit: null output");
-  return gemv_presplit(qtype, (const uint8_t*)d_w, n, k, m, d_workspace, d_bias, d_y, (cudaStream_t)stream);
+  return gemv_presplit(qtype, (const uint8_t*)d_w, n, k, m, d_workspace, true, d_bias, d_y, 0, (cudaStream_t)stream);
 }
 
 extern "C" int xm_qgemv(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k, const void* d_x,
@@ -933,38 +982,56 @@ extern "C" int xm_qgemv(int qtype, const void* d_w, int64_t w_bytes, int64_t n, 
     return xm_set_error(XM_ERR_INVALID, "qgemv: bad x dtype %d", x_dtype);
   if (n == 0) return XM_OK;
   if (!d_x || !d_y) return xm_set_error(XM_ERR_INVALID, "qgemv: null pointer");
-  if (((uintptr_t)d_x & 15) != 0) return xm_set_error(XM_ERR_INVALID, "qgemv: x not 16-byte aligned");
+  if (!aligned16(d_x)) return xm_set_error(XM_ERR_INVALID, "qgemv: x not 16-byte aligned");
   cudaStream_t st = (cudaStream_t)stream;
-  const bool fast = integer_path_type(qtype) && ((uintptr_t)d_w & 15) == 0 && d_workspace &&
-                    workspace_bytes >= xm_qgemv_workspace_size(k, m) && ((uintptr_t)d_workspace & 15) == 0;
-  if (integer_path_type(qtype) && lane_major_shape(m, k) && ((uintptr_t)d_w & 15) == 0) {
+  const uint8_t* W = (const uint8_t*)d_w;
+  if (qtype == T_Q4_K && lane_major_shape(m, k) && aligned16(d_w))
     // one row of 4096: the split is done inside the GEMV, no workspace needed
-    if (x_dtype == XM_DT_F32)
-      rc = launch_q4k_k4096_m1<float>((const uint8_t*)d_w, n, d_x, d_bias, d_y, st);
-    else if (x_dtype == XM_DT_BF16)
-      rc = launch_q4k_k4096_m1<__nv_bfloat16>((const uint8_t*)d_w, n, d_x, d_bias, d_y, st);
-    else
-      rc = launch_q4k_k4096_m1<__half>((const uint8_t*)d_w, n, d_x, d_bias, d_y, st);
-    if (rc) return rc;
-    return xm_check_launch("qgemv(integer, k4096 m1, fused split)");
-  }
-  if (fast) {
+    return k4096_fused(x_dtype, W, n, d_x, nullptr, 0.f, d_bias, d_y, 0, st);
+  const bool ws_ok =
+      d_workspace && workspace_bytes >= xm_qgemv_workspace_size(k, m) && aligned16(d_workspace);
+  if (ws_ok && aligned16(d_w) && integer_path(qtype, n, k, m)) {
     rc = split_activation(d_x, x_dtype, m, k, d_workspace, st);
     if (rc) return rc;
-    return gemv_presplit(qtype, (const uint8_t*)d_w, n, k, m, d_workspace, d_bias, d_y, st);
+    return gemv_presplit(qtype, W, n, k, m, d_workspace, true, d_bias, d_y, 0, st);
   }
+  return exact_path(qtype, W, n, k, d_x, x_dtype, m, d_bias, d_y, st);
+}
+
+extern "C" int xm_qgemv_ex(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k, const void* d_x,
+                           int x_dtype, int64_t m, int64_t x_stride, int prologue, const float* d_norm_w, float eps,
+                           const float* d_bias, float* d_y, int accumulate, void* d_workspace,
+                           int64_t workspace_bytes, void* stream) {
+  int64_t nb = 0;
+  int rc = check_gemv_args("qgemv_ex", qtype, d_w, w_bytes, n, k, m, &nb);
+  if (rc) return rc;
+  if (x_dtype != XM_DT_F32 && x_dtype != XM_DT_BF16 && x_dtype != XM_DT_F16)
+    return xm_set_error(XM_ERR_INVALID, "qgemv_ex: bad x dtype %d", x_dtype);
+  if (prologue != XM_PRO_NONE && prologue != XM_PRO_RMSNORM && prologue != XM_PRO_SWIGLU)
+    return xm_set_error(XM_ERR_INVALID, "qgemv_ex: unknown prologue %d", prologue);
+  if (prologue == XM_PRO_RMSNORM && !d_norm_w) return xm_set_error(XM_ERR_INVALID, "qgemv_ex: RMSNorm needs weights");
+  if (x_stride < (prologue == XM_PRO_SWIGLU ? 2 * k : k))
+    return xm_set_error(XM_ERR_INVALID, "qgemv_ex: x_stride %lld too small", (long long)x_stride);
+  if (n == 0) return XM_OK;
+  if (!d_x || !d_y) return xm_set_error(XM_ERR_INVALID, "qgemv_ex: null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
   const uint8_t* W = (const uint8_t*)d_w;
-  switch (m) {
-    case 1: launch_exact<1>(qtype, W, n, k, d_x, x_dtype, d_bias, d_y, st); break;
-    case 2: launch_exact<2>(qtype, W, n, k, d_x, x_dtype, d_bias, d_y, st); break;
-    case 3: launch_exact<3>(qtype, W, n, k, d_x, x_dtype, d_bias, d_y, st); break;
-    case 4: launch_exact<4>(qtype, W, n, k, d_x, x_dtype, d_bias, d_y, st); break;
-    case 5: launch_exact<5>(qtype, W, n, k, d_x, x_dtype, d_bias, d_y, st); break;
-    case 6: launch_exact<6>(qtype, W, n, k, d_x, x_dtype, d_bias, d_y, st); break;
-    case 7: launch_exact<7>(qtype, W, n, k, d_x, x_dtype, d_bias, d_y, st); break;
-    default: launch_exact<8>(qtype, W, n, k, d_x, x_dtype, d_bias, d_y, st); break;
+  if (qtype == T_Q4_K && lane_major_shape(m, k) && prologue != XM_PRO_SWIGLU && aligned16(d_w) && aligned16(d_x) &&
+      (prologue != XM_PRO_RMSNORM || aligned16(d_norm_w)))
+    return k4096_fused(x_dtype, W, n, d_x, prologue == XM_PRO_RMSNORM ? d_norm_w : nullptr, eps, d_bias, d_y,
+                       accumulate, st);
+  const bool ws_ok =
+      d_workspace && workspace_bytes >= xm_qgemv_workspace_size(k, m) && aligned16(d_workspace);
+  if (ws_ok && aligned16(d_w) && integer_path(qtype, n, k, m)) {
+    rc = split_rows(d_x, x_dtype, m, k, x_stride, prologue, d_norm_w, eps, d_workspace, st);
+    if (rc) return rc;
+    return gemv_presplit(qtype, W, n, k, m, d_workspace, false, d_bias, d_y, accumulate, st);
   }
-  return xm_check_launch("qgemv(exact)");
+  if (prologue == XM_PRO_NONE && !accumulate && x_stride == k && aligned16(d_x))
+    return exact_path(qtype, W, n, k, d_x, x_dtype, m, d_bias, d_y, st);
+  return xm_set_error(XM_ERR_UNSUPPORTED,
+                      "qgemv_ex: prologues and accumulate need the integer-dot path (Q4_K/Q5_K/Q6_K/Q8_0, "
+                      "16-byte aligned weights and a workspace)");
 }
 
 // Exact-path-only entry (used to cross-check the integer path on the same inputs).

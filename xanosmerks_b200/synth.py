@@ -76,3 +76,34 @@ def make_weight(name: str, n: int, k: int, seed: int = 0, dist: str = "config") 
         raise ValueError(f"{name}: k={k} is not a multiple of {QK[name]}")
     rng = np.random.default_rng(seed)
     return make_blocks(name, n * k // QK[name], rng, dist)
+
+
+def make_weight_device(name: str, n: int, k: int, seed: int = 0, device="cuda", scale: float | None = None):
+    """The ``"config"`` distribution of :func:`make_weight` generated on the GPU
+    (torch generator, so a 4.5 GB model takes a second rather than minutes):
+    a flat uint8 CUDA tensor of ``n * k / QK * record`` bytes.  ``scale``
+    replaces the distribution's scale factor of every fp16/fp32 scale field
+    (``|N(0,1)| * scale``), e.g. to give a decoder layer weights of a trained
+    model's magnitude.  The bytes differ from :func:`make_weight` for the same
+    seed (a different generator); copy them to the host to check them."""
+    import torch
+
+    if k % QK[name]:
+        raise ValueError(f"{name}: k={k} is not a multiple of {QK[name]}")
+    rec = RECORD[name]
+    nb = n * k // QK[name]
+    g = torch.Generator(device=device)
+    g.manual_seed(int(seed))
+    b = torch.randint(0, 256, (nb, rec), dtype=torch.uint8, device=device, generator=g)
+    if name == "Q8_0":
+        q = torch.randint(-127, 128, (nb, 32), dtype=torch.int16, device=device, generator=g)
+        b[:, 2:34] = q.to(torch.int8).view(torch.uint8)
+    for off, kind, (mode, s) in _FIELDS[name]:
+        s = s if scale is None else scale
+        v = torch.randn(nb, device=device, generator=g, dtype=torch.float32)
+        v = v.abs() * s if mode == "abs" else v * s
+        if kind == "f16":
+            b[:, off:off + 2] = v.to(torch.float16).view(torch.uint8).reshape(nb, 2)
+        else:
+            b[:, off:off + 4] = v.view(torch.uint8).reshape(nb, 4)
+    return b.reshape(-1)
