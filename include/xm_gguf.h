@@ -200,19 +200,17 @@ int xm_qgemv_noalloc(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int
  * (vocab rows of D) -- the reference indexes its dequantized embedding
  * (forward.py:151).
  *
- * xm_rope_append: for T tokens (token t of sequence seq[t] at position
- * pos[t]), qkv row t = [q | k | v] (Hq, Hk, Hk heads, fp32, row pitch
- * qkv_stride): rotate-half rotary embedding of q and k in place (angle
- * pos / theta^(2i/128)), and k, v appended to the caches at that position
- * (attention.py:66-70, KV append of attention.py:99-104).
- *
- * xm_attention: causal GQA attention of Lq (<= 8) new tokens per sequence
- * (tokens b*Lq + j of qkv; token j of sequence b sees keys 0 .. pos0[b] + j)
- * over the caches, out row b*Lq + j = softmax(q k^T / sqrt(128)) v per query
- * head (Hq / Hk <= 8 query heads share a KV head); attention.py:105-115 with
- * ninewas9's scaled_dot_product_attention.  Keys are split 64 per CTA; the
- * partial softmaxes meet in `d_workspace` (xm_attention_workspace_size bytes,
- * zeroed once before the first call; every call leaves it ready for the next).
+ * xm_attention: causal GQA attention of Lq (<= 8) new tokens per sequence.
+ * qkv row b*Lq + j = [q | k | v] (Hq, Hk, Hk heads, fp32, row pitch
+ * qkv_stride) of token j of sequence b at position pos0[b] + j, as the QKV
+ * projection produced it.  Fused: rotate-half rotary embedding of q and k
+ * (angle pos / theta^(2i/128), attention.py:66-70), append of the rotated k
+ * and of v to the caches (attention.py:99-104), and out row b*Lq + j =
+ * softmax(q k^T / sqrt(128) + causal mask) v per query head, Hq / Hk <= 8 query
+ * heads per KV head (attention.py:105-115 with ninewas9's
+ * scaled_dot_product_attention).  Keys are split 64 per CTA; the partial
+ * softmaxes meet in `d_workspace` (xm_attention_workspace_size bytes, zeroed
+ * once before the first call; every call leaves it ready for the next).
  *
  * xm_argmax: out[b] = first index of the maximum of logits row b (greedy
  * sampling, sampling.py:51-52 `sample_greedy`).
@@ -221,11 +219,9 @@ int xm_qgemv_noalloc(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int
  */
 int xm_embed(int qtype, const void* d_table, int64_t table_bytes, int64_t vocab, int64_t D, const int* d_ids,
              int64_t B, float* d_out, void* stream);
-int xm_rope_append(float* d_qkv, int64_t qkv_stride, const int* d_seq, const int* d_pos, int64_t T, int Hq, int Hk,
-                   int head_dim, float theta, int64_t max_ctx, void* d_kcache, void* d_vcache, void* stream);
 int64_t xm_attention_workspace_size(int64_t B, int Hk, int64_t max_ctx);
-int xm_attention(const float* d_qkv, int64_t qkv_stride, const void* d_kcache, const void* d_vcache,
-                 const int* d_pos0, int64_t B, int Lq, int Hq, int Hk, int head_dim, int64_t max_ctx, float* d_out,
+int xm_attention(const float* d_qkv, int64_t qkv_stride, void* d_kcache, void* d_vcache, const int* d_pos0, int64_t B,
+                 int Lq, int Hq, int Hk, int head_dim, float theta, int64_t max_ctx, float* d_out,
                  int64_t out_stride, void* d_workspace, int64_t workspace_bytes, void* stream);
 int xm_argmax(const float* d_logits, int64_t B, int64_t V, int* d_out, void* stream);
 

@@ -73,10 +73,11 @@ def test_host_side_validation_without_launch():
     assert L.xm_qgemv_ex(14, None, 0, 4, 256, None, 0, 1, 256, _lib.PRO_SWIGLU, None, 1e-5, None, None, 0, None,
                          0, None) == _lib.XM_ERR_INVALID
     # decoder kernels: head_dim other than 128 is unsupported, bad shapes are invalid
-    assert L.xm_rope_append(None, 0, None, None, 1, 32, 8, 64, 5e5, 16, None, None, None) == _lib.XM_ERR_UNSUPPORTED
-    assert L.xm_attention(None, 0, None, None, None, 1, 9, 32, 8, 128, 16, None, 0, None, 0,
+    assert L.xm_attention(None, 0, None, None, None, 1, 1, 32, 8, 64, 5e5, 16, None, 0, None, 0,
+                          None) == _lib.XM_ERR_UNSUPPORTED
+    assert L.xm_attention(None, 0, None, None, None, 1, 9, 32, 8, 128, 5e5, 16, None, 0, None, 0,
                           None) == _lib.XM_ERR_INVALID
-    assert L.xm_attention(None, 0, None, None, None, 1, 1, 32, 3, 128, 16, None, 0, None, 0,
+    assert L.xm_attention(None, 0, None, None, None, 1, 1, 32, 3, 128, 5e5, 16, None, 0, None, 0,
                           None) == _lib.XM_ERR_INVALID
     assert L.xm_embed(0, None, 0, 10, 4096, None, 1, None, None) == _lib.XM_ERR_UNSUPPORTED
     assert L.xm_argmax(None, 0, 10, None, None) == _lib.XM_ERR_INVALID

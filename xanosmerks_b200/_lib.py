@@ -46,10 +46,9 @@ SIGNATURES = {
     "xm_qgemv_ex": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _int, _i64, _i64, _int, _vp, _f32, _vp, _vp, _int,
                            _vp, _i64, _vp]),
     "xm_embed": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp]),
-    "xm_rope_append": (_int, [_vp, _i64, _vp, _vp, _i64, _int, _int, _int, _f32, _i64, _vp, _vp, _vp]),
     "xm_attention_workspace_size": (_i64, [_i64, _int, _i64]),
-    "xm_attention": (_int, [_vp, _i64, _vp, _vp, _vp, _i64, _int, _int, _int, _int, _i64, _vp, _i64, _vp, _i64,
-                            _vp]),
+    "xm_attention": (_int, [_vp, _i64, _vp, _vp, _vp, _i64, _int, _int, _int, _int, _f32, _i64, _vp, _i64, _vp,
+                            _i64, _vp]),
     "xm_argmax": (_int, [_vp, _i64, _i64, _vp, _vp]),
 }
 

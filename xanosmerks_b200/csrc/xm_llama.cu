@@ -1,8 +1,8 @@
 // Kernels around the quantized projections of a Llama-style decoder step:
-// embedding gather from GGUF blocks, rotary embedding fused with the KV-cache
-// append, grouped-query attention over the cache (split along the keys, the
-// partial softmaxes merged by the last CTA of each head group), and greedy
-// argmax.  RMSNorm, SwiGLU and the residual adds are fused into the GEMVs
+// embedding gather from GGUF blocks, grouped-query attention over the KV
+// cache with the rotary embedding and the cache append fused in (split along
+// the keys, the partial softmaxes merged by the last CTA of each head group),
+// and greedy argmax.  RMSNorm, SwiGLU and the residual adds are fused into the GEMVs
 // (xm_qgemv_ex).  These kernels move a few MB per step against the ~4.5 GB of
 // weight blocks the projections stream, so they are written for latency
 // (programmatic dependent launch, one wave) rather than bandwidth.
@@ -59,63 +59,46 @@ struct EmbedLaunch {
 };
 
 // ---------------------------------------------------------------------------
-// Rotary embedding + KV append.  qkv row t = [q (Hq x 128) | k (Hk x 128) |
-// v (Hk x 128)], fp32, token t of sequence seq[t] at position pos[t].  q and k
-// are rotated in place (out[i] = x[i] cos - x[i+64] sin, out[i+64] = x[i+64]
-// cos + x[i] sin, angle pos / theta^(2i/128)); k and v go to the fp16 caches
-// [B][Hk][max_ctx][128] at that position.  Grid (T, Hq + 2 Hk), 64 threads.
-// ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(64) k_rope_append(float* __restrict__ qkv, int64_t qkv_stride,
-                                                    const int* __restrict__ seq, const int* __restrict__ pos, int Hq,
-                                                    int Hk, float theta, int max_ctx, __half* __restrict__ kc,
-                                                    __half* __restrict__ vc) {
-  grid_dep_wait();
-  grid_dep_launch();
-  const int t = blockIdx.x, h = blockIdx.y, i = threadIdx.x;
-  float* row = qkv + (int64_t)t * qkv_stride;
-  const int p = pos[t];
-  float* v = row + (int64_t)h * kHeadDim;
-  float a = v[i], b = v[i + 64];
-  if (h < Hq + Hk) {
-    const float inv_freq = 1.0f / powf(theta, (float)(2 * i) / (float)kHeadDim);
-    float sn, cs;
-    sincosf((float)p * inv_freq, &sn, &cs);
-    const float ra = a * cs - b * sn, rb = b * cs + a * sn;
-    a = ra;
-    b = rb;
-    if (h < Hq) {
-      v[i] = a;
-      v[i + 64] = b;
-      return;
-    }
-  }
-  const int hk = h < Hq + Hk ? h - Hq : h - Hq - Hk;
-  __half* cache = h < Hq + Hk ? kc : vc;
-  const int64_t dst = (((int64_t)seq[t] * Hk + hk) * max_ctx + p) * kHeadDim;
-  cache[dst + i] = __float2half_rn(a);
-  cache[dst + i + 64] = __float2half_rn(b);
-}
-
-// ---------------------------------------------------------------------------
-// Attention for Lq new tokens of each of B sequences.  CTA (b, hk, s) covers
-// keys [64 s, 64 s + 64) of KV head hk of sequence b for all G = Hq/Hk query
-// heads and all Lq tokens (token j sees keys 0 .. pos0[b] + j).  It writes
-// its partial (max, sum, unnormalised output) per (j, g) to the workspace;
-// the last CTA of (b, hk) to finish merges the partials in split order and
-// writes out[b*Lq + j][hq][128].
+// Attention for Lq new tokens of each of B sequences, with the rotary
+// embedding and the KV-cache append fused in.
+//
+// qkv row b*Lq + j = [q (Hq x 128) | k (Hk x 128) | v (Hk x 128)] of token j
+// of sequence b, at position pos0[b] + j, as the QKV projection wrote it (not
+// yet rotated).  Rotary embedding (rotate-half): out[i] = x[i] cos - x[i+64]
+// sin, out[i+64] = x[i+64] cos + x[i] sin, angle = pos / theta^(2i/128).
+//
+// CTA (b, hk, s) covers keys [64 s, 64 s + 64) of KV head hk of sequence b,
+// for the G = Hq/Hk query heads of that KV head and every new token (token j
+// sees keys 0 .. pos0[b] + j).  Keys already in the cache come from it; the
+// new tokens' keys and values that fall in the CTA's range are rotated,
+// written to the cache and used from shared memory.  Each CTA rotates the
+// query rows itself, writes its partial (max, sum, unnormalised output) per
+// (token, head) to the workspace, and the last CTA of (b, hk) to finish merges
+// the partials in split order into out[b*Lq + j][hq][128].
 // ---------------------------------------------------------------------------
 struct AttnPart {
   float m, l;
 };
 
+constexpr int kKvPitch = kHeadDim / 2 + 1;   // half2 words per cached row in shared memory (conflict-free)
+
+XM_DEV void rope_pair(float& a, float& b, int pos, int i, float theta) {
+  const float inv_freq = 1.0f / powf(theta, (float)(2 * i) / (float)kHeadDim);
+  float sn, cs;
+  sincosf((float)pos * inv_freq, &sn, &cs);
+  const float ra = a * cs - b * sn, rb = b * cs + a * sn;
+  a = ra;
+  b = rb;
+}
+
 __global__ void __launch_bounds__(256) k_attention(const float* __restrict__ qkv, int64_t qkv_stride,
-                                                   const __half* __restrict__ kc, const __half* __restrict__ vc,
+                                                   __half* __restrict__ kc, __half* __restrict__ vc,
                                                    const int* __restrict__ pos0, int Lq, int Hq, int Hk, int max_ctx,
-                                                   int nsplit, float* __restrict__ part_o,
+                                                   int nsplit, float theta, float* __restrict__ part_o,
                                                    AttnPart* __restrict__ part_ml, int* __restrict__ tickets,
                                                    float* __restrict__ out, int64_t out_stride) {
-  __shared__ __align__(16) __half ks[kAttnKeys][kHeadDim + 8];
-  __shared__ __align__(16) __half vs[kAttnKeys][kHeadDim + 8];
+  __shared__ __half2 ks[kAttnKeys][kKvPitch];
+  __shared__ __half2 vs[kAttnKeys][kKvPitch];
   __shared__ __align__(16) float qs[kMaxGroup][kHeadDim];
   __shared__ float sc[kMaxGroup][kAttnKeys];
   __shared__ int last;
@@ -129,54 +112,90 @@ __global__ void __launch_bounds__(256) k_attention(const float* __restrict__ qkv
   const int kend = min(k0 + kAttnKeys, p0 + Lq);   // keys this CTA may need for its last token
   const float scale = rsqrtf((float)kHeadDim);
   const int64_t bh = (int64_t)b * Hk + hk;
+  __half* K = kc + bh * max_ctx * kHeadDim;
+  __half* V = vc + bh * max_ctx * kHeadDim;
+  const int kv_off = Hq * kHeadDim;                // k heads follow the q heads in a qkv row
 
   if (k0 < kend) {
-    // stage the key and value tile (16-byte loads)
-    const __half* K = kc + (bh * max_ctx + k0) * kHeadDim;
-    const __half* V = vc + (bh * max_ctx + k0) * kHeadDim;
     const int nk = kend - k0;
-    for (int i = tid; i < nk * (kHeadDim / 8); i += 256) {
+    // old keys (positions < p0) from the cache, 16-byte loads
+    const int nold = max(0, min(nk, p0 - k0));
+    for (int i = tid; i < nold * (kHeadDim / 8); i += 256) {
       const int r = i / (kHeadDim / 8), c = (i % (kHeadDim / 8)) * 8;
-      *reinterpret_cast<uint4*>(&ks[r][c]) = *reinterpret_cast<const uint4*>(K + (int64_t)r * kHeadDim + c);
-      *reinterpret_cast<uint4*>(&vs[r][c]) = *reinterpret_cast<const uint4*>(V + (int64_t)r * kHeadDim + c);
+      const uint4 kv = *reinterpret_cast<const uint4*>(K + (int64_t)(k0 + r) * kHeadDim + c);
+      const uint4 vv = *reinterpret_cast<const uint4*>(V + (int64_t)(k0 + r) * kHeadDim + c);
+      const __half2* k2 = reinterpret_cast<const __half2*>(&kv);
+      const __half2* v2 = reinterpret_cast<const __half2*>(&vv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        ks[r][c / 2 + e] = k2[e];
+        vs[r][c / 2 + e] = v2[e];
+      }
+    }
+    // new keys in range: rotate, append to the cache, keep in shared memory
+    for (int i = tid; i < (nk - nold) * (kHeadDim / 2); i += 256) {
+      const int r = nold + i / (kHeadDim / 2), d = i % (kHeadDim / 2);
+      const int pos = k0 + r, j = pos - p0;
+      const float* row = qkv + ((int64_t)b * Lq + j) * qkv_stride + kv_off;
+      float ka = row[hk * kHeadDim + d], kb = row[hk * kHeadDim + d + 64];
+      rope_pair(ka, kb, pos, d, theta);
+      const float va = row[(Hk + hk) * kHeadDim + d], vb = row[(Hk + hk) * kHeadDim + d + 64];
+      const __half hka = __float2half_rn(ka), hkb = __float2half_rn(kb);
+      const __half hva = __float2half_rn(va), hvb = __float2half_rn(vb);
+      K[(int64_t)pos * kHeadDim + d] = hka;
+      K[(int64_t)pos * kHeadDim + d + 64] = hkb;
+      V[(int64_t)pos * kHeadDim + d] = hva;
+      V[(int64_t)pos * kHeadDim + d + 64] = hvb;
+      reinterpret_cast<__half*>(&ks[r][0])[d] = hka;
+      reinterpret_cast<__half*>(&ks[r][0])[d + 64] = hkb;
+      reinterpret_cast<__half*>(&vs[r][0])[d] = hva;
+      reinterpret_cast<__half*>(&vs[r][0])[d + 64] = hvb;
     }
     for (int j = 0; j < Lq; ++j) {
       const int len = p0 + j + 1;                    // token j sees keys < len
       const int nkj = min(kend, len) - k0;           // keys of this tile it sees (may be <= 0)
       __syncthreads();                               // tiles staged / previous token done with qs, sc
-      for (int i = tid; i < G * kHeadDim; i += 256) {
-        const int g = i / kHeadDim, d = i % kHeadDim;
-        qs[g][d] = qkv[((int64_t)b * Lq + j) * qkv_stride + (int64_t)(hk * G + g) * kHeadDim + d];
+      // rotated query rows of the G heads
+      for (int i = tid; i < G * (kHeadDim / 2); i += 256) {
+        const int g = i / (kHeadDim / 2), d = i % (kHeadDim / 2);
+        const float* qr = qkv + ((int64_t)b * Lq + j) * qkv_stride + (int64_t)(hk * G + g) * kHeadDim;
+        float a = qr[d], c = qr[d + 64];
+        rope_pair(a, c, p0 + j, d, theta);
+        qs[g][d] = a * scale;
+        qs[g][d + 64] = c * scale;
       }
       __syncthreads();
-      // scores: warp w takes keys w*8 .. w*8+7; lanes over dims (4 each)
-      for (int kk = 0; kk < 8; ++kk) {
-        const int key = warp * 8 + kk;
-        if (key >= nkj) break;
-        const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&ks[key][4 * lane]));
-        const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&ks[key][4 * lane + 2]));
-        for (int g = 0; g < G; ++g) {
-          const float4 q4 = *reinterpret_cast<const float4*>(&qs[g][4 * lane]);
-          float d = q4.x * k01.x + q4.y * k01.y + q4.z * k23.x + q4.w * k23.y;
-          d = warp_sum(d);
-          if (lane == 0) sc[g][key] = d * scale;
+      if (nkj <= 0) continue;                        // uniform across the CTA
+      // scores: thread (head group, key); lanes over keys, q broadcast
+      {
+        const int key = tid & (kAttnKeys - 1);
+        for (int g = tid >> 6; g < G; g += 256 / kAttnKeys) {
+          float acc = 0.f;
+          if (key < nkj) {
+            const float2* q2 = reinterpret_cast<const float2*>(qs[g]);
+#pragma unroll 16
+            for (int w = 0; w < kHeadDim / 2; ++w) {
+              const float2 kf = __half22float2(ks[key][w]);
+              const float2 qf = q2[w];
+              acc = fmaf(qf.x, kf.x, acc);
+              acc = fmaf(qf.y, kf.y, acc);
+            }
+          }
+          sc[g][key] = key < nkj ? acc : -INFINITY;
         }
       }
       __syncthreads();
-      // per head: max and exp over the tile (warp g handles head g; G <= 8)
-      if (warp < G && nkj > 0) {
+      // per head: max and exp over the tile (warp g handles head g)
+      if (warp < G) {
         const int g = warp;
-        float mx = -INFINITY;
-        for (int key = lane; key < nkj; key += 32) mx = fmaxf(mx, sc[g][key]);
+        const float s0 = sc[g][lane], s1 = sc[g][lane + 32];
+        float mx = fmaxf(s0, s1);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float sum = 0.f;
-        for (int key = lane; key < nkj; key += 32) {
-          const float e = expf(sc[g][key] - mx);
-          sc[g][key] = e;
-          sum += e;
-        }
-        sum = warp_sum(sum);
+        const float e0 = lane < nkj ? expf(s0 - mx) : 0.f, e1 = lane + 32 < nkj ? expf(s1 - mx) : 0.f;
+        sc[g][lane] = e0;
+        sc[g][lane + 32] = e1;
+        const float sum = warp_sum(e0 + e1);
         if (lane == 0) {
           AttnPart pm;
           pm.m = mx;
@@ -185,23 +204,18 @@ __global__ void __launch_bounds__(256) k_attention(const float* __restrict__ qkv
         }
       }
       __syncthreads();
-      // unnormalised output: thread (g, 4 dims)
-      if (nkj > 0) {
-        for (int i = tid; i < G * (kHeadDim / 4); i += 256) {
-          const int g = i / (kHeadDim / 4), d = (i % (kHeadDim / 4)) * 4;
-          float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
-          for (int key = 0; key < nkj; ++key) {
-            const float pk = sc[g][key];
-            const float2 v01 = __half22float2(*reinterpret_cast<const __half2*>(&vs[key][d]));
-            const float2 v23 = __half22float2(*reinterpret_cast<const __half2*>(&vs[key][d + 2]));
-            o0 = fmaf(pk, v01.x, o0);
-            o1 = fmaf(pk, v01.y, o1);
-            o2 = fmaf(pk, v23.x, o2);
-            o3 = fmaf(pk, v23.y, o3);
-          }
-          *reinterpret_cast<float4*>(part_o + (((bh * nsplit + s) * kMaxLq + j) * kMaxGroup + g) * kHeadDim + d) =
-              make_float4(o0, o1, o2, o3);
+      // unnormalised output: thread (head, 2 dims); lanes over dims
+      for (int i = tid; i < G * (kHeadDim / 2); i += 256) {
+        const int g = i / (kHeadDim / 2), d2 = i % (kHeadDim / 2);
+        float o0 = 0.f, o1 = 0.f;
+        for (int key = 0; key < nkj; ++key) {
+          const float pk = sc[g][key];
+          const float2 vf = __half22float2(vs[key][d2]);
+          o0 = fmaf(pk, vf.x, o0);
+          o1 = fmaf(pk, vf.y, o1);
         }
+        *reinterpret_cast<float2*>(part_o + (((bh * nsplit + s) * kMaxLq + j) * kMaxGroup + g) * kHeadDim +
+                                   2 * d2) = make_float2(o0, o1);
       }
     }
   }
@@ -212,13 +226,13 @@ __global__ void __launch_bounds__(256) k_attention(const float* __restrict__ qkv
   __syncthreads();
   if (!last) return;
   __threadfence();
+  const float* mls = reinterpret_cast<const float*>(part_ml);
   for (int i = tid; i < Lq * G * (kHeadDim / 4); i += 256) {
     const int j = i / (G * (kHeadDim / 4));
     const int rem = i % (G * (kHeadDim / 4));
     const int g = rem / (kHeadDim / 4), d = (rem % (kHeadDim / 4)) * 4;
     const int len = p0 + j + 1;
     const int ns = min(nsplit, (len + kAttnKeys - 1) / kAttnKeys);
-    const float* mls = reinterpret_cast<const float*>(part_ml);
     float M = -INFINITY;
     for (int ss = 0; ss < ns; ++ss) M = fmaxf(M, __ldcg(&mls[2 * (((bh * nsplit + ss) * kMaxLq + j) * kMaxGroup + g)]));
     float L = 0.f;
@@ -240,7 +254,15 @@ __global__ void __launch_bounds__(256) k_attention(const float* __restrict__ qkv
   if (tid == 0) tickets[bh] = 0;   // ready for the next call
 }
 
-// first index of the maximum of each row (np.argmax semantics; NaN-free input)
+// first index of the maximum of each row (np.argmax semantics; NaN-free
+// input).  One CTA per row; 16-byte loads, eight in flight per thread.
+XM_DEV void argmax_take(float v, int i, float& best, int& idx) {
+  if (v > best || (v == best && i < idx)) {
+    best = v;
+    idx = i;
+  }
+}
+
 __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ logits, int V, int* __restrict__ out) {
   __shared__ float bv[32];
   __shared__ int bi[32];
@@ -250,20 +272,22 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ logit
   const float* r = logits + (int64_t)b * V;
   float best = -INFINITY;
   int idx = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float v = r[i];
-    if (v > best || (v == best && i < idx)) {
-      best = v;
-      idx = i;
-    }
+  const bool vec = (((uintptr_t)r) & 15) == 0;
+  const int V4 = vec ? V / 4 : 0;
+  const float4* r4 = reinterpret_cast<const float4*>(r);
+#pragma unroll 8
+  for (int i = threadIdx.x; i < V4; i += blockDim.x) {
+    const float4 v = __ldcs(r4 + i);
+    argmax_take(v.x, 4 * i, best, idx);
+    argmax_take(v.y, 4 * i + 1, best, idx);
+    argmax_take(v.z, 4 * i + 2, best, idx);
+    argmax_take(v.w, 4 * i + 3, best, idx);
   }
+  for (int i = 4 * V4 + threadIdx.x; i < V; i += blockDim.x) argmax_take(r[i], i, best, idx);
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, best, o);
     const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-    if (ov > best || (ov == best && oi < idx)) {
-      best = ov;
-      idx = oi;
-    }
+    argmax_take(ov, oi, best, idx);
   }
   if ((threadIdx.x & 31) == 0) {
     bv[threadIdx.x >> 5] = best;
@@ -271,11 +295,7 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ logit
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    for (int w = 1; w < (int)(blockDim.x + 31) / 32; ++w)
-      if (bv[w] > best || (bv[w] == best && bi[w] < idx)) {
-        best = bv[w];
-        idx = bi[w];
-      }
+    for (int w = 1; w < (int)(blockDim.x + 31) / 32; ++w) argmax_take(bv[w], bi[w], best, idx);
     out[b] = idx == 0x7fffffff ? 0 : idx;
   }
 }
@@ -317,31 +337,20 @@ int xm_embed(int qtype, const void* d_table, int64_t table_bytes, int64_t vocab,
   return launch_status(l.err, "embed");
 }
 
-int xm_rope_append(float* d_qkv, int64_t qkv_stride, const int* d_seq, const int* d_pos, int64_t T, int Hq, int Hk,
-                   int head_dim, float theta, int64_t max_ctx, void* d_kcache, void* d_vcache, void* stream) {
-  if (head_dim != kHeadDim) return xm_set_error(XM_ERR_UNSUPPORTED, "rope_append: head_dim %d (only 128)", head_dim);
-  if (T < 1 || Hq < 1 || Hk < 1 || qkv_stride < (int64_t)(Hq + 2 * Hk) * kHeadDim || max_ctx < 1 ||
-      max_ctx > (1 << 24) || !d_qkv || !d_seq || !d_pos || !d_kcache || !d_vcache)
-    return xm_set_error(XM_ERR_INVALID, "rope_append: bad arguments");
-  return launch_status(launch_pdl(k_rope_append, dim3((unsigned)T, (unsigned)(Hq + 2 * Hk)), dim3(64),
-                                  (cudaStream_t)stream, d_qkv, qkv_stride, d_seq, d_pos, Hq, Hk, theta, (int)max_ctx,
-                                  (__half*)d_kcache, (__half*)d_vcache),
-                       "rope_append");
-}
-
 int64_t xm_attention_workspace_size(int64_t B, int Hk, int64_t max_ctx) {
   const int64_t nsplit = (max_ctx + kAttnKeys - 1) / kAttnKeys;
   const int64_t cells = B * Hk * nsplit * kMaxLq * kMaxGroup;
   return cells * kHeadDim * 4 + cells * (int64_t)sizeof(AttnPart) + B * Hk * 4 + 256;
 }
 
-int xm_attention(const float* d_qkv, int64_t qkv_stride, const void* d_kcache, const void* d_vcache,
-                 const int* d_pos0, int64_t B, int Lq, int Hq, int Hk, int head_dim, int64_t max_ctx, float* d_out,
+int xm_attention(const float* d_qkv, int64_t qkv_stride, void* d_kcache, void* d_vcache, const int* d_pos0, int64_t B,
+                 int Lq, int Hq, int Hk, int head_dim, float theta, int64_t max_ctx, float* d_out,
                  int64_t out_stride, void* d_workspace, int64_t workspace_bytes, void* stream) {
   if (head_dim != kHeadDim) return xm_set_error(XM_ERR_UNSUPPORTED, "attention: head_dim %d (only 128)", head_dim);
   if (B < 1 || Lq < 1 || Lq > kMaxLq || Hq < 1 || Hk < 1 || Hq % Hk || Hq / Hk > kMaxGroup)
     return xm_set_error(XM_ERR_INVALID, "attention: bad head counts (G <= 8) or more than 8 new tokens");
-  if (max_ctx < 1 || out_stride < (int64_t)Hq * kHeadDim || !d_qkv || !d_kcache || !d_vcache || !d_pos0 || !d_out)
+  if (max_ctx < 1 || max_ctx > (1 << 24) || qkv_stride < (int64_t)(Hq + 2 * Hk) * kHeadDim ||
+      out_stride < (int64_t)Hq * kHeadDim || !d_qkv || !d_kcache || !d_vcache || !d_pos0 || !d_out)
     return xm_set_error(XM_ERR_INVALID, "attention: bad arguments");
   if (!d_workspace || workspace_bytes < xm_attention_workspace_size(B, Hk, max_ctx) || ((uintptr_t)d_workspace & 15))
     return xm_set_error(XM_ERR_INVALID, "attention: workspace too small or unaligned");
@@ -352,9 +361,9 @@ int xm_attention(const float* d_qkv, int64_t qkv_stride, const void* d_kcache, c
   int* tickets = (int*)(part_ml + cells);
   // tickets start at zero (the caller zeroes the workspace once) and every call leaves them at zero
   return launch_status(launch_pdl(k_attention, dim3((unsigned)(B * Hk), (unsigned)nsplit), dim3(256),
-                                  (cudaStream_t)stream, d_qkv, qkv_stride, (const __half*)d_kcache,
-                                  (const __half*)d_vcache, d_pos0, Lq, Hq, Hk, (int)max_ctx, nsplit, part_o, part_ml,
-                                  tickets, d_out, out_stride),
+                                  (cudaStream_t)stream, d_qkv, qkv_stride, (__half*)d_kcache, (__half*)d_vcache,
+                                  d_pos0, Lq, Hq, Hk, (int)max_ctx, nsplit, theta, part_o, part_ml, tickets, d_out,
+                                  out_stride),
                        "attention");
 }
 

@@ -13,15 +13,16 @@
 //
 // Structure (one CTA per SM): a producer warp streams whole rows into a ring
 // of shared-memory slots with cp.async.bulk (no multicast), R rows per copy;
-// 12 consumer warps take work items from shared counters.  A row is cut into
-// "units" of 128 elements (a half super-block, or four Q8_0 blocks); rows of
-// more than 32 units are cut into P = 2 or 4 parts, and consumer warp w always
-// serves part w % P, so with one activation row the digits of the lane's unit
-// stay in registers for the whole kernel.  A work item is one part of RI =
-// 32 / L rows (L lanes per row, one unit per lane); the P partial sums of a
-// row meet in shared memory and the warp that finishes last adds them in
-// part order (deterministic).  With 2..8 activation rows the digits live in
-// shared memory instead.
+// 8 consumer warps (224 registers per thread) take work items from shared
+// counters.  A row is cut into "units" of 128 elements (a half super-block, or
+// four Q8_0 blocks); rows of more than 32 units are cut into P = 2 or 4 parts,
+// and consumer warp w always serves part w % P, so with one activation row the
+// digits of the lane's unit stay in registers for the whole kernel.  A work
+// item is one part of RI = 2 * 32 / L rows (L lanes per row, one unit per
+// lane, two rows per lane: two independent dot products share the digits);
+// the P partial sums of a row meet in shared memory and the warp that finishes
+// last adds them in part order (deterministic).  With 2..8 activation rows the
+// digits live in shared memory instead.
 #include <algorithm>
 
 #include "xm_gemv_dot.cuh"
@@ -29,7 +30,7 @@
 
 namespace {
 
-constexpr int kKqConsumers = 12;
+constexpr int kKqConsumers = 8;    // + the producer: 288 threads, up to 224 registers each
 constexpr int kKqThreads = (kKqConsumers + 1) * 32;
 constexpr int kUnitX = 336;       // shared bytes per (activation row, unit): 256 B digits, 4 x float4, 16 B pad
 constexpr int kPieceBytes = 64;   // digits per 32-element group in the split workspace
@@ -39,8 +40,12 @@ constexpr int kMaxSmem = 227 * 1024;
 
 // ---------------------------------------------------------------------------
 // Per-type unit decoders.  load() pulls the unit's weight bytes out of the
-// shared-memory ring into registers; dot() is the contribution of the unit's
-// four 32-element groups for one activation row (digits via xf(j, x, ts)).
+// shared-memory ring into registers.  dot2() returns the dot products of two
+// units (two rows, same columns) with one activation row's digits of the
+// unit's four 32-element groups (x[j]: words 0-7 plane 0, 8-15 plane 1; ts[j] =
+// (t, s_lo, s_hi, s32)).  The integer loops run word-major over all groups and
+// both rows, so every dp4a chain is at most 4-8 deep and 16-32 chains are
+// independent.
 // ---------------------------------------------------------------------------
 template <int T> struct Unit;
 
@@ -62,27 +67,34 @@ template <> struct Unit<T_Q4_K> {
       qs[4 * i] = v.x; qs[4 * i + 1] = v.y; qs[4 * i + 2] = v.z; qs[4 * i + 3] = v.w;
     }
   }
-  template <typename XF>
-  XM_DEV float dot(XF&& xf) const {
-    float acc = 0.f, macc = 0.f;
+  XM_DEV static void dot2(const Unit (&w)[2], const uint32_t (&x)[4][16], const float4 (&ts)[4], float (&out)[2]) {
+    int D[2][4][2];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint32_t x[16];
-      float4 ts;
-      xf(j, x, ts);
-      int D0 = 0, D1 = 0;
+    for (int r = 0; r < 2; ++r)
 #pragma unroll
-      for (int w = 0; w < 8; ++w) {
-        const uint32_t q = qs[8 * (j >> 1) + w];
-        const uint32_t v = (j & 1) ? (q & 0xF0F0F0F0u) : (q & 0x0F0F0F0Fu);   // odd: 16x the code
-        D0 = dp4a_us(v, x[w], D0);
-        D1 = dp4a_us(v, x[8 + w], D1);
+      for (int j = 0; j < 4; ++j) D[r][j][0] = D[r][j][1] = 0;
+#pragma unroll
+    for (int wd = 0; wd < 8; ++wd)
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t q = w[r].qs[8 * (j >> 1) + wd];
+          const uint32_t v = (j & 1) ? (q & 0xF0F0F0F0u) : (q & 0x0F0F0F0Fu);   // odd: 16x the code
+          D[r][j][0] = dp4a_us(v, x[j][wd], D[r][j][0]);
+          D[r][j][1] = dp4a_us(v, x[j][8 + wd], D[r][j][1]);
+        }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      float a = 0.f, b = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float P = __int2float_rn(254 * D[r][j][0] + D[r][j][1]);
+        a = fmaf(byte_f(w[r].scw, j) * ((j & 1) ? 0.0625f * ts[j].x : ts[j].x), P, a);
+        b = fmaf(byte_f(w[r].mnw, j), ts[j].w, b);
       }
-      const float P = __int2float_rn(254 * D0 + D1);
-      acc = fmaf(byte_f(scw, j) * ((j & 1) ? 0.0625f * ts.x : ts.x), P, acc);
-      macc = fmaf(byte_f(mnw, j), ts.w, macc);
+      out[r] = w[r].d * a - w[r].dmin * b;
     }
-    return d * acc - dmin * macc;
   }
 };
 
@@ -108,31 +120,37 @@ template <> struct Unit<T_Q5_K> {
       qs[4 * i] = v.x; qs[4 * i + 1] = v.y; qs[4 * i + 2] = v.z; qs[4 * i + 3] = v.w;
     }
   }
-  template <typename XF>
-  XM_DEV float dot(XF&& xf) const {
-    float acc = 0.f, macc = 0.f;
+  XM_DEV static void dot2(const Unit (&w)[2], const uint32_t (&x)[4][16], const float4 (&ts)[4], float (&out)[2]) {
+    int D[2][4][2];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint32_t x[16];
-      float4 ts;
-      xf(j, x, ts);
-      const uint32_t hb = qh[j >> 1];
-      int D0 = 0, D1 = 0;
+    for (int r = 0; r < 2; ++r)
 #pragma unroll
-      for (int w = 0; w < 8; ++w) {
-        const uint32_t q = qs[8 * (j >> 1) + w];
-        const uint32_t nib = (j & 1) ? ((q >> 4) & 0x0F0F0F0Fu) : (q & 0x0F0F0F0Fu);
-        // bits 4w..4w+3 of hb -> bit 4 of bytes 0..3 (the four partial products do not overlap)
-        const uint32_t fifth = (((hb >> (4 * w)) & 0xFu) * 0x02040810u) & 0x10101010u;
-        const uint32_t v = nib | fifth;
-        D0 = dp4a_us(v, x[w], D0);
-        D1 = dp4a_us(v, x[8 + w], D1);
+      for (int j = 0; j < 4; ++j) D[r][j][0] = D[r][j][1] = 0;
+#pragma unroll
+    for (int wd = 0; wd < 8; ++wd)
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t q = w[r].qs[8 * (j >> 1) + wd];
+          const uint32_t nib = (j & 1) ? ((q >> 4) & 0x0F0F0F0Fu) : (q & 0x0F0F0F0Fu);
+          // bits 4wd..4wd+3 of the high-bit word -> bit 4 of bytes 0..3 (partial products do not overlap)
+          const uint32_t fifth = (((w[r].qh[j >> 1] >> (4 * wd)) & 0xFu) * 0x02040810u) & 0x10101010u;
+          const uint32_t v = nib | fifth;
+          D[r][j][0] = dp4a_us(v, x[j][wd], D[r][j][0]);
+          D[r][j][1] = dp4a_us(v, x[j][8 + wd], D[r][j][1]);
+        }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      float a = 0.f, b = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float P = __int2float_rn(254 * D[r][j][0] + D[r][j][1]);
+        a = fmaf(byte_f(w[r].scw, j) * ts[j].x, P, a);
+        b = fmaf(byte_f(w[r].mnw, j), ts[j].w, b);
       }
-      const float P = __int2float_rn(254 * D0 + D1);
-      acc = fmaf(byte_f(scw, j) * ts.x, P, acc);
-      macc = fmaf(byte_f(mnw, j), ts.w, macc);
+      out[r] = w[r].d * a - w[r].dmin * b;
     }
-    return d * acc - dmin * macc;
   }
 };
 
@@ -143,50 +161,48 @@ template <> struct Unit<T_Q5_K> {
 // are read with aligned 32-bit loads joined by funnel shifts.
 template <> struct Unit<T_Q6_K> {
   float d;
-  const uint8_t* qlp;   // ql half (64 B), read 32 B at a time inside dot()
-  uint32_t qh[8], sc[2];
+  uint32_t ql[16], qh[8], sc[2];
   XM_DEV static const uint8_t* rec(const uint8_t* row, int u) { return row + (u >> 1) * 210; }
   XM_DEV void load(const uint8_t* r, int h) {
-    qlp = r + 64 * h;
+    lds_words<16>(r + 64 * h, ql);
     lds_words<8>(r + 128 + 32 * h, qh);
     lds_words<2>(r + 192 + 8 * h, sc);
     d = __half2float(*reinterpret_cast<const __half*>(r + 208));
   }
-  template <typename XF>
-  XM_DEV float dot(XF&& xf) const {
-    float acc = 0.f;
+  XM_DEV static void dot2(const Unit (&w)[2], const uint32_t (&x)[4][16], const float4 (&ts)[4], float (&out)[2]) {
+    int D[2][4][2][2];   // [row][group][half of 16][plane]
 #pragma unroll
-    for (int jj = 0; jj < 2; ++jj) {   // groups jj and jj + 2 share 32 bytes of ql (low / high nibbles)
-      uint32_t ql[8];
-      lds_words<8>(qlp + 32 * jj, ql);
+    for (int r = 0; r < 2; ++r)
 #pragma unroll
-      for (int jh = 0; jh < 2; ++jh) {
-        const int j = jj + 2 * jh;
-        uint32_t x[16];
-        float4 ts;
-        xf(j, x, ts);
-        int A0 = 0, A1 = 0, B0 = 0, B1 = 0;
+      for (int j = 0; j < 4; ++j) D[r][j][0][0] = D[r][j][0][1] = D[r][j][1][0] = D[r][j][1][1] = 0;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) {
-          const uint32_t nib = jh ? ((ql[w] >> 4) & 0x0F0F0F0Fu) : (ql[w] & 0x0F0F0F0Fu);
-          const uint32_t hq = qh[w];
-          const uint32_t hp = j == 0 ? (hq << 4) : j == 1 ? (hq << 2) : j == 2 ? hq : (hq >> 2);
-          const uint32_t v = nib | (hp & 0x30303030u);
-          if (w < 4) {
-            A0 = dp4a_us(v, x[w], A0);
-            A1 = dp4a_us(v, x[8 + w], A1);
-          } else {
-            B0 = dp4a_us(v, x[w], B0);
-            B1 = dp4a_us(v, x[8 + w], B1);
-          }
+    for (int wd = 0; wd < 8; ++wd)
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const uint32_t l0 = w[r].ql[wd], l1 = w[r].ql[8 + wd], hq = w[r].qh[wd];
+        const uint32_t v[4] = {(l0 & 0x0F0F0F0Fu) | ((hq << 4) & 0x30303030u),
+                               (l1 & 0x0F0F0F0Fu) | ((hq << 2) & 0x30303030u),
+                               ((l0 >> 4) & 0x0F0F0F0Fu) | (hq & 0x30303030u),
+                               ((l1 >> 4) & 0x0F0F0F0Fu) | ((hq >> 2) & 0x30303030u)};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          D[r][j][wd >> 2][0] = dp4a_us(v[j], x[j][wd], D[r][j][wd >> 2][0]);
+          D[r][j][wd >> 2][1] = dp4a_us(v[j], x[j][8 + wd], D[r][j][wd >> 2][1]);
         }
-        const float PA = __int2float_rn(254 * A0 + A1), PB = __int2float_rn(254 * B0 + B1);
-        const float sa = sbyte_f(sc[j >> 1], (2 * j) & 3), sb = sbyte_f(sc[j >> 1], (2 * j + 1) & 3);
-        acc = fmaf(sa, fmaf(ts.x, PA, -32.0f * ts.y), acc);
-        acc = fmaf(sb, fmaf(ts.x, PB, -32.0f * ts.z), acc);
       }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      float a = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float PA = __int2float_rn(254 * D[r][j][0][0] + D[r][j][0][1]);
+        const float PB = __int2float_rn(254 * D[r][j][1][0] + D[r][j][1][1]);
+        const float sa = sbyte_f(w[r].sc[j >> 1], (2 * j) & 3), sb = sbyte_f(w[r].sc[j >> 1], (2 * j + 1) & 3);
+        a = fmaf(sa, fmaf(ts[j].x, PA, -32.0f * ts[j].y), a);
+        a = fmaf(sb, fmaf(ts[j].x, PB, -32.0f * ts[j].z), a);
+      }
+      out[r] = w[r].d * a;
     }
-    return d * acc;
   }
 };
 
@@ -203,23 +219,28 @@ template <> struct Unit<T_Q8_0> {
       lds_words<8>(r + 34 * b + 2, qs[b]);
     }
   }
-  template <typename XF>
-  XM_DEV float dot(XF&& xf) const {
-    float acc = 0.f;
+  XM_DEV static void dot2(const Unit (&w)[2], const uint32_t (&x)[4][16], const float4 (&ts)[4], float (&out)[2]) {
+    int D[2][4][2];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint32_t x[16];
-      float4 ts;
-      xf(j, x, ts);
-      int D0 = 0, D1 = 0;
+    for (int r = 0; r < 2; ++r)
 #pragma unroll
-      for (int w = 0; w < 8; ++w) {
-        D0 = dp4a_ss(qs[j][w], x[w], D0);
-        D1 = dp4a_ss(qs[j][w], x[8 + w], D1);
-      }
-      acc = fmaf(d[j] * ts.x, __int2float_rn(254 * D0 + D1), acc);
+      for (int j = 0; j < 4; ++j) D[r][j][0] = D[r][j][1] = 0;
+#pragma unroll
+    for (int wd = 0; wd < 8; ++wd)
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          D[r][j][0] = dp4a_ss(w[r].qs[j][wd], x[j][wd], D[r][j][0]);
+          D[r][j][1] = dp4a_ss(w[r].qs[j][wd], x[j][8 + wd], D[r][j][1]);
+        }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      float a = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) a = fmaf(w[r].d[j] * ts[j].x, __int2float_rn(254 * D[r][j][0] + D[r][j][1]), a);
+      out[r] = a;
     }
-    return acc;
   }
 };
 
@@ -251,7 +272,8 @@ __global__ void __launch_bounds__(kKqThreads, 1) k_qgemv_kq(const __grid_constan
   const int rb = q0 * a.R;
   const int nrows = min(a.N, q1 * a.R) - rb;
   const int nch = q1 - q0;
-  const int RI = 32 / a.L;
+  const int RL = 32 / a.L;          // rows covered by the warp's lanes at once
+  const int RI = 2 * RL;             // rows per work item (each lane takes two)
   const int ngroups = (nrows + RI - 1) / RI;
   grid_dep_launch();   // the next kernel only prefetches its weights before its own wait
 
@@ -329,6 +351,8 @@ __global__ void __launch_bounds__(kKqThreads, 1) k_qgemv_kq(const __grid_constan
     asm volatile("bar.sync 1, %0;" ::"r"(kKqConsumers * 32) : "memory");   // consumer warps only
   }
 
+  // a work item: rows row0 + lane/L and row0 + lane/L + RL (two independent
+  // dot products per lane), one part of each
   for (;;) {
     int gi = 0;
     if (lane == 0) gi = atomicAdd(&part_next[p], 1);
@@ -337,66 +361,77 @@ __global__ void __launch_bounds__(kKqThreads, 1) k_qgemv_kq(const __grid_constan
     const int row0 = gi * RI, q = row0 / a.R, slot = q % a.S;
     smem_wait_eq(&slot_tag[slot], q);   // armed for this chunk, not the previous lap
     mbar_wait_bounded(&full[slot], (uint32_t)((q / a.S) & 1));
-    const int row = row0 + lane / a.L;
-    float acc[M];
-#pragma unroll
-    for (int m = 0; m < M; ++m) acc[m] = 0.f;
-    if (uvalid && row < nrows) {
-      const uint8_t* rowp = ring + (size_t)slot * a.slot_bytes + (size_t)(row - q * a.R) * a.RB;
-      Unit<T> w;
-      w.load(Unit<T>::rec(rowp, u), h);
-      if constexpr (M == 1) {
-        acc[0] = w.dot([&](int j, uint32_t(&x)[16], float4& t4) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) x[i] = xr[j][i];
-          t4 = tr[j];
-        });
-      } else {
-#pragma unroll
-        for (int m = 0; m < M; ++m) {
-          const uint8_t* xu = xs + ((size_t)m * a.U + u) * kUnitX;
-          acc[m] = w.dot([&](int j, uint32_t(&x)[16], float4& t4) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const uint4 v = lds_v4(xu + 64 * j + 16 * i);
-              x[4 * i] = v.x; x[4 * i + 1] = v.y; x[4 * i + 2] = v.z; x[4 * i + 3] = v.w;
-            }
-            t4 = *reinterpret_cast<const float4*>(xu + 256 + 16 * j);
-          });
-        }
-      }
-    }
+    const int rowA = row0 + lane / a.L, rowB = rowA + RL;
+    const bool okA = uvalid && rowA < nrows, okB = uvalid && rowB < nrows;
+    const uint8_t* base = ring + (size_t)slot * a.slot_bytes;
+    Unit<T> w2[2];
+    if (okA) w2[0].load(Unit<T>::rec(base + (size_t)(rowA - q * a.R) * a.RB, u), h);
+    if (okB) w2[1].load(Unit<T>::rec(base + (size_t)(rowB - q * a.R) * a.RB, u), h);
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);   // every lane has read its weights
+    if (lane == 0) mbar_arrive(&empty[slot]);   // every lane holds its weights in registers
+    float accA[M], accB[M];
 #pragma unroll
     for (int m = 0; m < M; ++m) {
-      float v = acc[m];
-      for (int o = a.L >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      acc[m] = v;
-    }
-    if (c == 0 && row < nrows) {
-      const int64_t grow = rb + row;
-      if (a.P == 1) {
-#pragma unroll
-        for (int m = 0; m < M; ++m) {
-          float v = acc[m] + (a.bias ? a.bias[grow] : 0.f);
-          if (a.accumulate) v = a.y[(int64_t)m * a.N + grow] + v;
-          a.y[(int64_t)m * a.N + grow] = v;
-        }
+      float o2[2];
+      if constexpr (M == 1) {
+        Unit<T>::dot2(w2, xr, tr, o2);
       } else {
+        // lanes past the row's last unit read unit 0 (their result is dropped)
+        const uint8_t* xu = xs + ((size_t)m * a.U + (uvalid ? u : 0)) * kUnitX;
+        uint32_t x[4][16];
+        float4 t4[4];
 #pragma unroll
-        for (int m = 0; m < M; ++m) part[((size_t)row * a.P + p) * M + m] = acc[m];
-        __threadfence_block();
-        if (atomicAdd(&row_cnt[row], 1) == a.P - 1) {
-          __threadfence_block();
+        for (int j = 0; j < 4; ++j) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 v = lds_v4(xu + 64 * j + 16 * i);
+            x[j][4 * i] = v.x; x[j][4 * i + 1] = v.y; x[j][4 * i + 2] = v.z; x[j][4 * i + 3] = v.w;
+          }
+          t4[j] = *reinterpret_cast<const float4*>(xu + 256 + 16 * j);
+        }
+        Unit<T>::dot2(w2, x, t4, o2);
+      }
+      accA[m] = okA ? o2[0] : 0.f;
+      accB[m] = okB ? o2[1] : 0.f;
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      float va = accA[m], vb = accB[m];
+      for (int o = a.L >> 1; o > 0; o >>= 1) {
+        va += __shfl_xor_sync(0xffffffffu, va, o);
+        vb += __shfl_xor_sync(0xffffffffu, vb, o);
+      }
+      accA[m] = va;
+      accB[m] = vb;
+    }
+    if (c == 0) {
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int row = k ? rowB : rowA;
+        if (row >= nrows) continue;
+        const int64_t grow = rb + row;
+        if (a.P == 1) {
 #pragma unroll
           for (int m = 0; m < M; ++m) {
-            const volatile float* pr = part + (size_t)row * a.P * M + m;
-            float v = pr[0];
-            for (int pp = 1; pp < a.P; ++pp) v += pr[pp * M];
-            v += a.bias ? a.bias[grow] : 0.f;
+            float v = (k ? accB[m] : accA[m]) + (a.bias ? a.bias[grow] : 0.f);
             if (a.accumulate) v = a.y[(int64_t)m * a.N + grow] + v;
             a.y[(int64_t)m * a.N + grow] = v;
+          }
+        } else {
+#pragma unroll
+          for (int m = 0; m < M; ++m) part[((size_t)row * a.P + p) * M + m] = k ? accB[m] : accA[m];
+          __threadfence_block();
+          if (atomicAdd(&row_cnt[row], 1) == a.P - 1) {
+            __threadfence_block();
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+              const volatile float* pr = part + (size_t)row * a.P * M + m;
+              float v = pr[0];
+              for (int pp = 1; pp < a.P; ++pp) v += pr[pp * M];
+              v += a.bias ? a.bias[grow] : 0.f;
+              if (a.accumulate) v = a.y[(int64_t)m * a.N + grow] + v;
+              a.y[(int64_t)m * a.N + grow] = v;
+            }
           }
         }
       }
@@ -411,6 +446,10 @@ __global__ void __launch_bounds__(kKqThreads, 1) k_qgemv_kq(const __grid_constan
 //   XM_PRO_SWIGLU   v = silu(x[:K]) * x[K:2K]             (forward.py:97-98, primitives.py:37-44)
 // Output: the group-major split (digits [m][G][64], (t, s_lo, s_hi, s32) [m][G]).
 // ---------------------------------------------------------------------------
+// Grid (rows, ceil(G / kSplitGroups)): each CTA splits kSplitGroups groups of
+// its row (with RMSNorm every CTA first reduces the whole row, 16-56 KB from L2).
+constexpr int kSplitGroups = 16;
+
 template <typename XT, int PRO>
 __global__ void __launch_bounds__(256) k_split_rows(const XT* __restrict__ x, int64_t x_stride, int K,
                                                     const float* __restrict__ norm_w, float eps,
@@ -421,6 +460,7 @@ __global__ void __launch_bounds__(256) k_split_rows(const XT* __restrict__ x, in
   const int m = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const XT* xr = x + (int64_t)m * x_stride;
   const int G = K / 32;
+  const int g_begin = blockIdx.y * kSplitGroups, g_end = min(G, g_begin + kSplitGroups);
   float rms = 1.f;
   if constexpr (PRO == XM_PRO_RMSNORM) {
     float ss = 0.f;
@@ -436,7 +476,7 @@ __global__ void __launch_bounds__(256) k_split_rows(const XT* __restrict__ x, in
     for (int w = 0; w < 8; ++w) tot += red[w];
     rms = sqrtf(tot / (float)K + eps);
   }
-  for (int g = warp; g < G; g += 8) {
+  for (int g = g_begin + warp; g < g_end; g += 8) {
     const int k = g * 32 + lane;
     float v;
     if constexpr (PRO == XM_PRO_SWIGLU) {
@@ -525,7 +565,7 @@ bool plan(int qtype, int64_t n, int64_t k, int64_t m, KqArgs& a, int& smem) {
   const int UP = (U + P - 1) / P;
   int L = 1;
   while (L < UP) L <<= 1;
-  const int RI = 32 / L;
+  const int RI = 2 * (32 / L);   // rows per work item
   const int64_t RB = k / qk_of(qtype) * rec;
   int r0 = 1;
   while ((r0 * RB) % 16) r0 <<= 1;
@@ -604,7 +644,7 @@ int split_rows(const void* d_x, int x_dtype, int64_t m, int64_t k, int64_t x_str
   int8_t* pieces = (int8_t*)d_ws;
   float4* ts = (float4*)((uint8_t*)d_ws + m * (k / 32) * kPieceBytes);
   cudaError_t e = cudaSuccess;
-  const dim3 grid((unsigned)m), block(256);
+  const dim3 grid((unsigned)m, (unsigned)((k / 32 + kSplitGroups - 1) / kSplitGroups)), block(256);
 #define XM_SPLIT(XT)                                                                                            \
   switch (prologue) {                                                                                           \
     case XM_PRO_RMSNORM:                                                                                        \

@@ -6,9 +6,9 @@ The B200 counterpart of the reference's decode loop: ``TransformerModel`` /
 sampling.py:51-52).  Every projection runs on the quantized blocks through the
 C ABI (``xm_qgemv_ex``: the attention RMSNorm is fused into the QKV GEMV, the
 MLP RMSNorm into the gate/up GEMV, SwiGLU into the down GEMV, the residual adds
-into the O and down GEMVs), plus four small kernels (embedding gather, RoPE +
-KV append, attention, argmax).  A decode step is ~7 launches per layer and is
-captured once into a CUDA graph.
+into the O and down GEMVs), plus three small kernels (embedding gather,
+attention with RoPE and the KV append fused in, argmax).  A decode step is 5-6
+launches per layer and is captured once into a CUDA graph.
 
 Layout: per layer the Q, K, V rows are concatenated into one GGUF tensor (one
 GEMV), and so are gate and up; the caches are fp16 ``[B][Hk][max_ctx][128]``.
@@ -208,8 +208,6 @@ class LlamaDecoder:
         self.ids = torch.zeros(rows, **i32)               # token ids of the rows being processed
         self.next_ids = torch.zeros(self.B, **i32)
         self.pos0 = torch.zeros(self.B, **i32)            # tokens already in the cache per sequence
-        self.tok_seq = torch.zeros(rows, **i32)
-        self.tok_pos = torch.zeros(rows, **i32)
         self.kc = torch.zeros(cfg.num_layers, self.B, self.hk, self.max_ctx, hd, dtype=torch.float16, device=dev)
         self.vc = torch.zeros_like(self.kc)
         aws = lib.xm_attention_workspace_size(self.B, self.hk, self.max_ctx)
@@ -248,14 +246,11 @@ class LlamaDecoder:
         for li, lw in enumerate(self.w.layers):
             # attention block (forward.py:107-111)
             self._gemv(lw["qkv"], self.h, rows, self.qkv, PRO_RMSNORM, lw["attn_norm"])
-            check(lib.xm_rope_append(self.qkv.data_ptr(), self.qkv_dim, self.tok_seq.data_ptr(),
-                                     self.tok_pos.data_ptr(), rows, self.hq, self.hk, cfg.head_dim,
-                                     cfg.rope_theta, self.max_ctx, self.kc[li].data_ptr(), self.vc[li].data_ptr(),
-                                     st), "rope_append")
             check(lib.xm_attention(self.qkv.data_ptr(), self.qkv_dim, self.kc[li].data_ptr(),
                                    self.vc[li].data_ptr(), self.pos0.data_ptr(), B, lq, self.hq, self.hk,
-                                   cfg.head_dim, self.max_ctx, self.attn.data_ptr(), self.hq * cfg.head_dim,
-                                   self.attn_ws.data_ptr(), self.attn_ws.numel(), st), "attention")
+                                   cfg.head_dim, cfg.rope_theta, self.max_ctx, self.attn.data_ptr(),
+                                   self.hq * cfg.head_dim, self.attn_ws.data_ptr(), self.attn_ws.numel(), st),
+                  "attention")
             if self.world == 1:
                 self._gemv(lw["o"], self.attn, rows, self.h, accumulate=True)
             else:
@@ -283,10 +278,10 @@ class LlamaDecoder:
         check(lib.xm_argmax(self.logits.data_ptr(), self.B, self.cfg.vocab_size, self.next_ids.data_ptr(),
                             self._stream()), "argmax")
 
-    def _embed(self, rows):
+    def _embed(self, rows, ids):
         e = self.w.embed
         check(lib.xm_embed(e.qtype.type_id, e.data.data_ptr(), e.nbytes, e.shape[0], e.shape[1],
-                           self.ids.data_ptr(), rows, self.h.data_ptr(), self._stream()), "embed")
+                           ids.data_ptr(), rows, self.h.data_ptr(), self._stream()), "embed")
 
     # -- public API -------------------------------------------------------
     def reset(self):
@@ -306,10 +301,7 @@ class LlamaDecoder:
         if lo < 0 or hi >= self.cfg.vocab_size:
             raise ValueError(f"token ids must lie in [0, {self.cfg.vocab_size}), got [{lo}, {hi}]")
         self.ids[:rows].copy_(ids.reshape(-1).to(self.dev, torch.int32))
-        ar = torch.arange(lq, device=self.dev, dtype=torch.int32)
-        self.tok_seq[:rows].copy_(torch.arange(B, device=self.dev, dtype=torch.int32).repeat_interleave(lq))
-        self.tok_pos[:rows].copy_((self.pos0[:, None] + ar[None, :]).reshape(-1))
-        self._embed(rows)
+        self._embed(rows, self.ids)
         self._layers(lq)
         self._head(lq)
         self.pos0.add_(lq)
@@ -331,10 +323,7 @@ class LlamaDecoder:
     def decode_step(self):
         """One greedy step from device state: the token in next_ids enters at pos0."""
         B = self.B
-        self.ids[:B].copy_(self.next_ids)
-        self.tok_seq[:B].copy_(torch.arange(B, device=self.dev, dtype=torch.int32))
-        self.tok_pos[:B].copy_(self.pos0)
-        self._embed(B)
+        self._embed(B, self.next_ids)
         self._layers(1)
         self._head(1)
         self.pos0.add_(1)
