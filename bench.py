@@ -59,6 +59,9 @@ def parse():
     ap.add_argument("--no-sweep", action="store_true", help="skip the prefill (tensor-core GEMM) sweep")
     ap.add_argument("--moe", action="store_true",
                     help="only time the Mixtral-shape MoE block (8 experts, top-2, 1024 tokens, 4096 -> 14336)")
+    ap.add_argument("--no-decode", action="store_true", help="skip the Llama decode tok/s section")
+    ap.add_argument("--no-moe", action="store_true", help="skip the MoE block section")
+    ap.add_argument("--decode-steps", type=int, default=64)
     ap.add_argument("--gemm-m", type=int, default=0,
                     help="only time the prefill GEMM with this many activation rows (profiling mode)")
     return ap.parse_args()
@@ -344,6 +347,9 @@ def run_ours(args):
         cpu = {"value": round(W_BYTES / dt / 1e9, 3), "unit": UNIT, "cores": blas_threads(), "kind": "port",
                "sample": f"{it} steps of fp32 (1x{K}) @ ({K}x{N}) numpy/BLAS on the dequantized weight (~10 s)"}
 
+    decode = None if args.no_decode else decode_section(args, rank, world, dev, peaks)
+    moe = None if (args.no_moe or world > 1) else moe_section(dev)
+
     if rank == 0:
         out = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
                "warmup": args.warmup, "ms_per_step": round(ms_steps / args.steps, 6), "higher_is_better": True,
@@ -351,12 +357,111 @@ def run_ours(args):
                "config": config({"max_rel_err_vs_exact_path": err}), "e2e": e2e, "roofline": roofline,
                "cpu_baseline": cpu, "clocks": clocks, "gpu_launches": args.steps,
                "prefill_sweep": {"metric": f"{QTYPE} {N}x{K} dequant-GEMM TFLOPS (bf16 x, fp16-exact weights)",
-                                 "points": sweep}}
+                                 "points": sweep},
+               "decode": decode, "moe": moe}
         print(json.dumps(out), flush=True)
     del g_steps
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def decode_section(args, rank, world, dev, peaks):
+    """Llama decode tok/s (32 layers, d 4096, GQA 32/8, FFN 14336, vocab 32000;
+    Q4_K attention and gate/up, Q6_K down and output): prompt of 512 random ids,
+    then greedy decode steps replayed from a CUDA graph.  With N ranks the model
+    is tensor-parallel over all of them (NCCL all-reduce of the row-parallel
+    partial sums), so per-step work is fixed as N grows (strong scaling)."""
+    import torch
+    import torch.distributed as dist
+    from xanosmerks_b200.llama import LlamaConfig, LlamaDecoder, LlamaWeights, synth_llama_weights
+    cfg = LlamaConfig()
+    full = synth_llama_weights(cfg, seed=11, device=dev)
+    weights = LlamaWeights.from_full(cfg, full, rank, world)
+    del full
+    torch.cuda.empty_cache()
+    bpt = cfg.weight_bytes_per_token()
+    res = {"model": "Llama 32L d4096 GQA32/8 FFN14336 V32000 (Q4_K attn+gate/up, Q6_K down+output; random-init)",
+           "prompt": 512, "tensor_parallel": world, "weight_bytes_per_token": bpt, "points": {}}
+    steps = max(16, min(args.decode_steps, 120))
+    st = torch.cuda.current_stream(dev)
+    for B in (1, 8):
+        dec = LlamaDecoder(weights, batch=B, max_ctx=640)
+        ids = torch.from_numpy(np.random.default_rng(12).integers(0, cfg.vocab_size, size=(B, 512)))
+        dec.prefill(ids)
+        dec.decode_step()
+        dec.length += 1
+        dec.capture()
+        dec.replay(2)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        dec.replay(steps)
+        e1.record(st)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        ms_tok = ms / steps
+        # end to end: each step's token ids come from pinned host memory and the next ids go back to it
+        pin_in = torch.zeros(B, dtype=torch.int32).pin_memory()
+        pin_out = torch.zeros(B, dtype=torch.int32).pin_memory()
+        pin_in.copy_(dec.next_ids.cpu())
+        e2e_steps = min(steps, 640 - dec.length - 1)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            dec.next_ids.copy_(pin_in, non_blocking=True)
+            dec.replay(1)
+            pin_out.copy_(dec.next_ids, non_blocking=True)
+            st.synchronize()
+            pin_in.copy_(pin_out)
+        t_e2e = time.perf_counter() - t0
+        if world > 1:
+            t = torch.tensor([t_e2e], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            t_e2e = float(t.item())
+        gbps = bpt / world / (ms_tok / 1e3) / 1e9
+        res["points"][f"batch{B}"] = {
+            "tok_s": round(B * 1000.0 / ms_tok, 1), "ms_per_step": round(ms_tok, 4),
+            "weight_GBps_per_gpu": round(gbps, 1),
+            "hbm_frac_of_measured": round(gbps / float(peaks.get("hbm_gbs", 6650.0)), 4),
+            "e2e_tok_s": round(B * e2e_steps / t_e2e, 1), "e2e_h2d_bytes_per_step": 4 * B,
+            "e2e_d2h_bytes_per_step": 4 * B}
+        dec.graph = None
+        del dec
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    del weights
+    torch.cuda.empty_cache()
+    return res
+
+
+def moe_section(dev):
+    import torch
+    layer, x, flops = moe_case(dev)
+    for _ in range(2):
+        layer.forward_device(x)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 5
+    e0.record()
+    for _ in range(reps):
+        layer.forward_device(x)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    del layer
+    torch.cuda.empty_cache()
+    return {"block": "Mixtral-shape MoE, 8 experts top-2, 1024 bf16 tokens, 4096->14336 SwiGLU, Q4_K experts",
+            "us": round(us, 1), "TFLOPS": round(flops / us / 1e6, 1), "tokens_per_s": round(1024 / us * 1e6, 1)}
 
 
 def run_gemm_only(args):

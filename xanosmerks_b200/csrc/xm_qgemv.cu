@@ -70,7 +70,10 @@ XM_DEV uint4 ldg_v4(const void* p) {
 XM_DEV uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xFF; }
 
 // y = v, or y += v for the residual-add (accumulate) form
-XM_DEV void store_out(float* p, float v, int accumulate) { *p = accumulate ? *p + v : v; }
+XM_DEV void store_out(float* p, float v, int accumulate) {
+  if (accumulate) v += *p;
+  *p = v;
+}
 
 // ---------------------------------------------------------------------------
 // Q4_K integer-dot GEMV.  A warp serves 4 rows; 8 lanes per row, lane cl
@@ -473,13 +476,15 @@ XM_DEV void split_row4096_to_smem(const XT* x, uint8_t* xsm, int tid, const floa
 }
 
 // XT = void: the split comes from a workspace written by k_split_x (lane-major);
-// otherwise x itself is read and split in the prologue.
-template <typename XT>
+// otherwise x itself is read and split in the prologue.  ACC: y += W x (the
+// residual add) instead of y = W x; a template flag so that the plain form
+// never reads y.
+template <typename XT, bool ACC>
 __global__ void __launch_bounds__(kWsThreads, 1) k_qgemv_q4k_k4096_m1(const uint8_t* __restrict__ W, int N,
                                                                       const void* __restrict__ xin,
                                                                       const float* __restrict__ norm_w, float eps,
                                                                       const float* __restrict__ bias,
-                                                                      float* __restrict__ y, int accumulate) {
+                                                                      float* __restrict__ y) {
   extern __shared__ __align__(128) uint8_t ws_smem[];
   uint8_t* slots = ws_smem;                                            // [kWsSlots][kWsSlotBytes]
   uint8_t* xsm = ws_smem + kWsSlots * kWsSlotBytes;                    // lane-major digits
@@ -587,20 +592,23 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_qgemv_q4k_k4096_m1(const uint
     float v = __shfl_xor_sync(0xffffffffu, upper ? v0 : v1, 16) + (upper ? v1 : v0);
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0) store_out(&y[rb + r], v + (bias ? bias[rb + r] : 0.f), accumulate);
-    if (lane == 16 && two) store_out(&y[rb + r + 1], v + (bias ? bias[rb + r + 1] : 0.f), accumulate);
+    if (lane == 0 || (lane == 16 && two)) {
+      const int row = rb + r + (lane >> 4);
+      const float o = v + (bias ? bias[row] : 0.f);
+      if constexpr (ACC) y[row] += o; else y[row] = o;
+    }
   }
 }
 
-template <typename XT>
-int launch_q4k_k4096_m1(const uint8_t* W, int64_t N, const void* xin, const float* norm_w, float eps,
-                        const float* bias, float* y, int accumulate, cudaStream_t st) {
+template <typename XT, bool ACC>
+int launch_q4k_k4096_m1_impl(const uint8_t* W, int64_t N, const void* xin, const float* norm_w, float eps,
+                             const float* bias, float* y, cudaStream_t st) {
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaError_t e =
-        cudaFuncSetAttribute(k_qgemv_q4k_k4096_m1<XT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kWsSmem);
+    cudaError_t e = cudaFuncSetAttribute(k_qgemv_q4k_k4096_m1<XT, ACC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kWsSmem);
     if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemv: smem attribute: %s", cudaGetErrorString(e));
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
@@ -615,9 +623,16 @@ int launch_q4k_k4096_m1(const uint8_t* W, int64_t N, const void* xin, const floa
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k_qgemv_q4k_k4096_m1<XT>, W, (int)N, xin, norm_w, eps, bias, y, accumulate);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_qgemv_q4k_k4096_m1<XT, ACC>, W, (int)N, xin, norm_w, eps, bias, y);
   if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemv launch: %s", cudaGetErrorString(e));
   return XM_OK;
+}
+
+template <typename XT>
+int launch_q4k_k4096_m1(const uint8_t* W, int64_t N, const void* xin, const float* norm_w, float eps,
+                        const float* bias, float* y, int accumulate, cudaStream_t st) {
+  return accumulate ? launch_q4k_k4096_m1_impl<XT, true>(W, N, xin, norm_w, eps, bias, y, st)
+                    : launch_q4k_k4096_m1_impl<XT, false>(W, N, xin, norm_w, eps, bias, y, st);
 }
 
 int q4k_tma_smem(int64_t m, int64_t nb) {
