@@ -370,8 +370,9 @@ def decode_section(args, rank, world, dev, peaks):
     """Llama decode tok/s (32 layers, d 4096, GQA 32/8, FFN 14336, vocab 32000;
     Q4_K attention and gate/up, Q6_K down and output): prompt of 512 random ids,
     then greedy decode steps replayed from a CUDA graph.  With N ranks the model
-    is tensor-parallel over all of them (NCCL all-reduce of the row-parallel
-    partial sums), so per-step work is fixed as N grows (strong scaling)."""
+    is tensor-parallel over all of them (the row-parallel partial sums are
+    all-reduced over NVLink peer memory), so per-step work is fixed as N grows
+    (strong scaling)."""
     import torch
     import torch.distributed as dist
     from xanosmerks_b200.llama import LlamaConfig, LlamaDecoder, LlamaWeights, synth_llama_weights
@@ -434,7 +435,7 @@ def decode_section(args, rank, world, dev, peaks):
             "hbm_frac_of_measured": round(gbps / float(peaks.get("hbm_gbs", 6650.0)), 4),
             "e2e_tok_s": round(B * e2e_steps / t_e2e, 1), "e2e_h2d_bytes_per_step": 4 * B,
             "e2e_d2h_bytes_per_step": 4 * B}
-        dec.graph = None
+        dec.close()
         del dec
         torch.cuda.synchronize()
         if world > 1:

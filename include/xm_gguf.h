@@ -225,6 +225,34 @@ int xm_attention(const float* d_qkv, int64_t qkv_stride, void* d_kcache, void* d
                  int64_t out_stride, void* d_workspace, int64_t workspace_bytes, void* stream);
 int xm_argmax(const float* d_logits, int64_t B, int64_t V, int* d_out, void* stream);
 
+/*
+ * Tensor-parallel exchange over NVLink peer memory (one process per GPU of a
+ * node): the all-reduce of the row-parallel partial sums of the O and down
+ * projections, added to the replicated residual stream (forward.py:111, :116
+ * with those projections split over K).
+ *
+ * xm_comm_create allocates this rank's communication buffer for vectors of up
+ * to max_elems fp32 values (xm_comm_buffer_size bytes) and returns an opaque
+ * comm and a 64-byte CUDA IPC handle; the ranks exchange the handles (any
+ * host channel) and each calls xm_comm_open_peer for every other rank.
+ * xm_allreduce_add(comm, h, part, n): h[i] += sum over ranks r (in rank order,
+ * identical on every rank) of part_r[i], for n <= max_elems (n % 4 == 0,
+ * 16-byte aligned pointers).  One kernel of `nctas` CTAs per call; CTA j of
+ * every rank exchanges the same slice with plain peer stores and per-(CTA,
+ * rank) flags (no multicast), waits for the other ranks' flags for at most
+ * 2 s (then sets XM_DEVERR_TIMEOUT in xm_device_status), and leaves the
+ * buffer ready for the next call, so calls can be captured into CUDA graphs.
+ * Every rank must make the same calls in the same order.  xm_comm_destroy
+ * closes the peer mappings and frees the buffer; call it on every rank after
+ * all ranks have finished their last xm_allreduce_add (host barrier + device
+ * synchronisation).  These entry points have no counterpart in the reference.
+ */
+int64_t xm_comm_buffer_size(int64_t max_elems);
+int xm_comm_create(int world, int rank, int64_t max_elems, int nctas, void** out_comm, void* out_handle);
+int xm_comm_open_peer(void* comm, int peer_rank, const void* handle);
+int xm_comm_destroy(void* comm);
+int xm_allreduce_add(void* comm, float* d_h, const float* d_part, int64_t n_elems, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,7 +1,7 @@
 """Worker for the tensor-parallel decoder check (one process per GPU, NCCL).
 
 Run as ``python -m torch.distributed.run --nproc-per-node N tests/tp_worker.py
-OUT.json``: every rank builds the same seeded weights, shards them, prefills a
+OUT.json [batch] [p2p|nccl]``: every rank builds the same seeded weights, shards them, prefills a
 prompt and decodes a few steps (eagerly and from a captured CUDA graph); rank 0
 also runs the unsharded decoder on its GPU and writes the normwise logit
 differences and token agreement to OUT.json.  Test infrastructure only.
@@ -30,15 +30,17 @@ def rel(a, b):
 def main():
     out_path = sys.argv[1]
     batch = int(sys.argv[2]) if len(sys.argv) > 2 else 2
+    collective = sys.argv[3] if len(sys.argv) > 3 else "p2p"
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     rank, world = dist.get_rank(), dist.get_world_size()
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
     cfg = LlamaConfig(num_layers=2, vocab_size=4096)
     full = synth_llama_weights(cfg, seed=5, device="cuda")
-    dec = LlamaDecoder(LlamaWeights.from_full(cfg, full, rank, world), batch=batch, max_ctx=64)
+    dec = LlamaDecoder(LlamaWeights.from_full(cfg, full, rank, world), batch=batch, max_ctx=64,
+                       collective=collective)
     ref = LlamaDecoder(LlamaWeights.from_full(cfg, full), batch=batch, max_ctx=64) if rank == 0 else None
     ids = torch.from_numpy(np.random.default_rng(6).integers(0, cfg.vocab_size, size=(batch, 9)))
-    report = {"world": world, "batch": batch, "steps": []}
+    report = {"world": world, "batch": batch, "collective": collective, "steps": []}
 
     def compare(tag):
         if rank == 0:
@@ -73,7 +75,7 @@ def main():
     toks = [torch.zeros_like(dec.next_ids) for _ in range(world)]
     dist.all_gather(toks, dec.next_ids)
     report["ranks_agree"] = all(torch.equal(t, toks[0]) for t in toks)
-    dec.graph = None   # release the graph holding NCCL calls before tearing the group down
+    dec.close()   # releases the graph (it may hold NCCL calls) and the peer-memory buffers
     torch.cuda.synchronize()
     dist.barrier()
     if rank == 0:

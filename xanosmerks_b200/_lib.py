@@ -50,6 +50,11 @@ SIGNATURES = {
     "xm_attention": (_int, [_vp, _i64, _vp, _vp, _vp, _i64, _int, _int, _int, _int, _f32, _i64, _vp, _i64, _vp,
                             _i64, _vp]),
     "xm_argmax": (_int, [_vp, _i64, _i64, _vp, _vp]),
+    "xm_comm_buffer_size": (_i64, [_i64]),
+    "xm_comm_create": (_int, [_int, _int, _i64, _int, ctypes.POINTER(_vp), _vp]),
+    "xm_comm_open_peer": (_int, [_vp, _int, _vp]),
+    "xm_comm_destroy": (_int, [_vp]),
+    "xm_allreduce_add": (_int, [_vp, _vp, _vp, _i64, _vp]),
 }
 
 

@@ -176,12 +176,18 @@ class LlamaDecoder:
     last token -> layers -> output head -> argmax), reading and writing only
     device state, so that it can be captured into a CUDA graph
     (``capture()`` / ``replay()``).  ``process_group``: the tensor-parallel group
-    (NCCL) when the weights are a shard of ``world > 1``.
+    when the weights are a shard of ``world > 1``; ``collective`` selects the
+    exchange of the row-parallel partial sums: ``"p2p"`` (default: the one-shot
+    all-reduce over NVLink peer memory of ``xm_allreduce_add``, buffers shared
+    through CUDA IPC) or ``"nccl"`` (``torch.distributed.all_reduce``).  Call
+    ``close()`` on every rank before tearing the process group down.
     """
 
     LQ_MAX = 8
+    COMM_CTAS = 16
 
-    def __init__(self, weights: LlamaWeights, batch: int, max_ctx: int, device=None, process_group=None):
+    def __init__(self, weights: LlamaWeights, batch: int, max_ctx: int, device=None, process_group=None,
+                 collective: str = "p2p"):
         cfg = weights.cfg
         self.cfg, self.w, self.B, self.max_ctx = cfg, weights, int(batch), int(max_ctx)
         self.world = weights.world
@@ -216,6 +222,40 @@ class LlamaDecoder:
         self.gemv_ws = torch.zeros(lib.xm_qgemv_workspace_size(kmax, 8) + 4096, dtype=torch.uint8, device=dev)
         self.graph = None
         self.length = 0
+        self.comm = None
+        if collective not in ("p2p", "nccl"):
+            raise ValueError(f"collective must be 'p2p' or 'nccl', got {collective!r}")
+        self.collective = collective
+        if self.world > 1 and collective == "p2p":
+            self._open_comm(rows * D)
+
+    def _open_comm(self, max_elems):
+        import ctypes
+
+        import torch.distributed as dist
+        rank = self.w.rank
+        comm = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * 64)()
+        with torch.cuda.device(self.dev):
+            check(lib.xm_comm_create(self.world, rank, max_elems, self.COMM_CTAS, ctypes.byref(comm), handle),
+                  "comm_create")
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=self.pg)
+            for r, hb in enumerate(handles):
+                buf = (ctypes.c_ubyte * 64).from_buffer_copy(hb)
+                check(lib.xm_comm_open_peer(comm, r, buf), "comm_open_peer")
+        self.comm = comm
+        dist.barrier(group=self.pg)
+
+    def close(self):
+        """Release the CUDA graph and the peer-memory buffers (every rank, after its last step)."""
+        self.graph = None
+        if self.comm is not None:
+            import torch.distributed as dist
+            torch.cuda.synchronize(self.dev)
+            dist.barrier(group=self.pg)           # no rank still writes into another's buffer
+            check(lib.xm_comm_destroy(self.comm), "comm_destroy")
+            self.comm = None
 
     # -- launches ---------------------------------------------------------
     def _stream(self):
@@ -234,6 +274,11 @@ class LlamaDecoder:
 
     def _allreduce_add(self, rows):
         """h[:rows] += sum over ranks of part[:rows] (row-parallel outputs)."""
+        if self.comm is not None:
+            n = rows * self.cfg.hidden_size
+            check(lib.xm_allreduce_add(self.comm, self.h.data_ptr(), self.part.data_ptr(), n, self._stream()),
+                  "allreduce_add")
+            return
         import torch.distributed as dist
         p = self.part[:rows]
         dist.all_reduce(p, group=self.pg)
