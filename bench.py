@@ -348,7 +348,7 @@ def run_ours(args):
                "sample": f"{it} steps of fp32 (1x{K}) @ ({K}x{N}) numpy/BLAS on the dequantized weight (~10 s)"}
 
     decode = None if args.no_decode else decode_section(args, rank, world, dev, peaks)
-    moe = None if (args.no_moe or world > 1) else moe_section(dev)
+    moe = None if args.no_moe else (moe_section(dev) if world == 1 else moe_ep_section(dev, rank, world))
 
     if rank == 0:
         out = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -443,6 +443,50 @@ def decode_section(args, rank, world, dev, peaks):
     del weights
     torch.cuda.empty_cache()
     return res
+
+
+def moe_ep_section(dev, rank, world, T=1024, E=8, k=2, H=4096, F=14336, seed=0):
+    """Mixtral-shape block with experts sharded over the ranks (E / N each) and
+    T tokens per rank exchanged with all-to-all (weak scaling: tokens per rank
+    fixed); the same seeded weights as the single-GPU section."""
+    import torch
+    import torch.distributed as dist
+    from xanosmerks_b200.moe import MoELayerEP
+    from xanosmerks_b200.ops import GGUFTensor
+    from xanosmerks_b200.synth import make_weight
+    rng = np.random.default_rng(seed)
+    gate = rng.standard_normal((E, H)).astype(np.float32) * 0.02
+    weights = {"gate": {"weight": gate}, "experts": {}}
+    el = E // world
+    for e in range(rank * el, (rank + 1) * el):
+        weights["experts"][str(e)] = {
+            wn: {"weight": GGUFTensor(make_weight("Q4_K", *shape, seed=seed * 1000 + 3 * e + i), "Q4_K", shape,
+                                      device=dev)}
+            for i, (wn, shape) in enumerate((("w1", (F, H)), ("w3", (F, H)), ("w2", (H, F))))}
+    layer = MoELayerEP({"num_experts": E, "num_experts_per_tok": k, "hidden_act": "silu"}, weights, rank, world)
+    x = torch.from_numpy(np.random.default_rng(100 + rank).standard_normal((T, H)).astype(np.float32)).to(dev).to(
+        torch.bfloat16)
+    for _ in range(2):
+        layer.forward_device(x)
+    torch.cuda.synchronize()
+    dist.barrier()
+    reps = 5
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        layer.forward_device(x)
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) * 1e3 / reps], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    us = float(t.item())
+    del layer
+    torch.cuda.empty_cache()
+    flops = 2.0 * T * world * k * 3 * F * H
+    return {"block": f"Mixtral-shape MoE, expert-parallel over {world} GPUs ({E // world} experts each), "
+                     f"{T} bf16 tokens per GPU, NCCL all-to-all exchange, Q4_K experts",
+            "us": round(us, 1), "TFLOPS_total": round(flops / us / 1e6, 1),
+            "tokens_per_s": round(T * world / us * 1e6, 1), "scaling": "weak"}
 
 
 def moe_section(dev):

@@ -178,6 +178,35 @@ int xm_moe_forward(const void* d_x, int x_dtype, int64_t T, int64_t H, const flo
                    int64_t workspace_bytes, void* stream);
 
 /*
+ * Expert parallelism: xm_moe_forward split at its two exchange points, for
+ * experts sharded over ranks (rank r owns experts [r*E/R, (r+1)*E/R)).
+ *
+ * xm_moe_dispatch routes the T local tokens (router, top-k, softmax, stable
+ * sort by expert: moe.py:61-93), writes the T*k selected rows of x in expert
+ * order to d_send ([T*k][H], x's element type; the rows for rank r's experts
+ * are therefore contiguous) and the per-expert row counts to d_cnt [E].  The
+ * caller exchanges counts and rows (all-to-all) and runs
+ * xm_moe_experts on the received rows: G groups of rows [off[g], off[g] +
+ * cnt[g]) (device arrays; typically one group per (source rank, local
+ * expert)) through the SwiGLU expert of group g (host pointer arrays h_w1,
+ * h_w3, h_w2 of G entries; Q4_K), fp32 rows out; max_rows bounds cnt[g].
+ * After exchanging the result rows back into the send order, xm_moe_combine
+ * forms out[t] = sum over the token's k rows, ascending expert, of row *
+ * weight (moe.py:110-113), reading the routing from the dispatch workspace
+ * (the same d_ws, xm_moe_workspace_size(T, H, F, E, k) bytes).  These entry
+ * points have no C counterpart in the reference (its MoELayer is one process).
+ */
+int xm_moe_dispatch(const void* d_x, int x_dtype, int64_t T, int64_t H, const float* d_gate, int E, int k,
+                    int64_t F, void* d_send, int* d_cnt, void* d_workspace, int64_t workspace_bytes, void* stream);
+int64_t xm_moe_experts_workspace_size(int64_t P, int64_t H, int64_t F);
+int xm_moe_experts(const void* d_rows, int x_dtype, int64_t P, int64_t H, int64_t F, int G, const int* d_cnt,
+                   const int* d_off, const void* const* h_w1, const void* const* h_w3, const void* const* h_w2,
+                   int qtype, int64_t max_rows, float* d_out, void* d_workspace, int64_t workspace_bytes,
+                   void* stream);
+int xm_moe_combine(const float* d_rows, int64_t T, int64_t H, int E, int k, int64_t F, const void* d_workspace,
+                   float* d_out, void* stream);
+
+/*
  * xm_qgemv without a workspace argument, for callers that cannot allocate
  * device memory (a host runtime that owns the allocator, a process that must
  * not allocate after start-up).  The activation split lives in a fixed array

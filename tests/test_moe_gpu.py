@@ -65,3 +65,46 @@ def test_moe_argument_checks(golden_moe):
         _layer_from_golden(g, 0)
     with pytest.raises(ValueError):
         _layer_from_golden(g, 5)
+
+
+@pytest.mark.parametrize("T,E,k,H,F,shards", [(300, 8, 2, 1024, 2048, 1), (200, 8, 2, 512, 768, 2),
+                                               (96, 8, 1, 256, 512, 4)])
+def test_split_entry_points_match_fused(T, E, k, H, F, shards):
+    """xm_moe_dispatch -> (exchange, emulated here on one GPU for `shards`
+    ranks: rows regrouped as (source rank, local expert)) -> xm_moe_experts ->
+    xm_moe_combine gives the same output as xm_moe_forward."""
+    import ctypes
+
+    from xanosmerks_b200._lib import DT_BF16, check, lib
+    gate, raws = _random_moe(E, H, F, seed=9)
+    weights = {"gate": {"weight": gate}, "experts": {}}
+    for e in range(E):
+        weights["experts"][str(e)] = {
+            wn: {"weight": GGUFTensor(raws[(e, wn)], "Q4_K", shape)}
+            for wn, shape in (("w1", (F, H)), ("w3", (F, H)), ("w2", (H, F)))}
+    layer = MoELayer({"num_experts": E, "num_experts_per_tok": k}, weights)
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(10)).to(torch.bfloat16).cuda()
+    ref = layer.forward_device(x)
+    st = torch.cuda.current_stream().cuda_stream
+    ws = torch.zeros(lib.xm_moe_workspace_size(T, H, F, E, k), dtype=torch.uint8, device="cuda")
+    send = torch.empty(T * k, H, dtype=torch.bfloat16, device="cuda")
+    cnt = torch.empty(E, dtype=torch.int32, device="cuda")
+    check(lib.xm_moe_dispatch(x.data_ptr(), DT_BF16, T, H, layer.gate.data_ptr(), E, k, F, send.data_ptr(),
+                              cnt.data_ptr(), ws.data_ptr(), ws.numel(), st), "dispatch")
+    c = cnt.cpu()
+    assert int(c.sum()) == T * k
+    # one rank holds all experts here; the groups are the experts themselves
+    off = (torch.cumsum(c, 0) - c).to(torch.int32)
+    G = E
+    p1 = (ctypes.c_void_p * G)(*[layer.w1[g].data.data_ptr() for g in range(G)])
+    p3 = (ctypes.c_void_p * G)(*[layer.w3[g].data.data_ptr() for g in range(G)])
+    p2 = (ctypes.c_void_p * G)(*[layer.w2[g].data.data_ptr() for g in range(G)])
+    rows = torch.empty(T * k, H, dtype=torch.float32, device="cuda")
+    ews = torch.empty(lib.xm_moe_experts_workspace_size(T * k, H, F), dtype=torch.uint8, device="cuda")
+    check(lib.xm_moe_experts(send.data_ptr(), DT_BF16, T * k, H, F, G, c.cuda().data_ptr(), off.cuda().data_ptr(),
+                             p1, p3, p2, 12, int(c.max()), rows.data_ptr(), ews.data_ptr(), ews.numel(), st), "experts")
+    out = torch.empty(T, H, dtype=torch.float32, device="cuda")
+    check(lib.xm_moe_combine(rows.data_ptr(), T, H, E, k, F, ws.data_ptr(), out.data_ptr(), st), "combine")
+    torch.cuda.synchronize()
+    assert rel_err(out.cpu().numpy(), ref.cpu().numpy()) < 1e-6
+    assert shards >= 1

@@ -50,6 +50,11 @@ SIGNATURES = {
     "xm_attention": (_int, [_vp, _i64, _vp, _vp, _vp, _i64, _int, _int, _int, _int, _f32, _i64, _vp, _i64, _vp,
                             _i64, _vp]),
     "xm_argmax": (_int, [_vp, _i64, _i64, _vp, _vp]),
+    "xm_moe_dispatch": (_int, [_vp, _int, _i64, _i64, _vp, _int, _int, _i64, _vp, _vp, _vp, _i64, _vp]),
+    "xm_moe_experts_workspace_size": (_i64, [_i64, _i64, _i64]),
+    "xm_moe_experts": (_int, [_vp, _int, _i64, _i64, _i64, _int, _vp, _vp, ctypes.POINTER(_vp), ctypes.POINTER(_vp),
+                              ctypes.POINTER(_vp), _int, _i64, _vp, _vp, _i64, _vp]),
+    "xm_moe_combine": (_int, [_vp, _i64, _i64, _int, _int, _i64, _vp, _vp, _vp]),
     "xm_comm_buffer_size": (_i64, [_i64]),
     "xm_comm_create": (_int, [_int, _int, _i64, _int, ctypes.POINTER(_vp), _vp]),
     "xm_comm_open_peer": (_int, [_vp, _int, _vp]),

@@ -147,7 +147,7 @@ __global__ void __launch_bounds__(256) k_moe_gather_prep(const XT* __restrict__ 
                                                          float* __restrict__ ascale) {
   const int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (p >= P) return;
-  const XT* xr = x + (int64_t)sorted_tok[p] * H;
+  const XT* xr = x + (int64_t)(sorted_tok ? sorted_tok[p] : p) * H;
   float amax = 0.f;
   for (int i = lane; i < H; i += 32) amax = fmaxf(amax, fabsf(to_f32(xr[i])));
 #pragma unroll
@@ -162,6 +162,16 @@ __global__ void __launch_bounds__(256) k_moe_gather_prep(const XT* __restrict__ 
   __half* o = a16 + (int64_t)p * H;
   for (int i = lane; i < H; i += 32) o[i] = __float2half_rn(to_f32(xr[i]) * inv);
   if (lane == 0) ascale[p] = ldexpf(1.0f, sh);
+}
+
+// send[p] = x[sorted_tok[p]] (rows in expert order, x's element type kept)
+template <typename XT>
+__global__ void __launch_bounds__(256) k_moe_gather(const XT* __restrict__ x, const int* __restrict__ sorted_tok, int P,
+                                                    int H, XT* __restrict__ send) {
+  const int p = blockIdx.y;
+  const XT* xr = x + (int64_t)sorted_tok[p] * H;
+  XT* o = send + (int64_t)p * H;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < H; i += gridDim.x * blockDim.x) o[i] = xr[i];
 }
 
 // silu(g) * u (primitives.py:37-44: x / (1 + exp(-x)) times up), then the
@@ -261,17 +271,81 @@ extern "C" int64_t xm_moe_workspace_size(int64_t T, int64_t H, int64_t F, int E,
   return carve(nullptr, T, H, F, E, k).bytes;
 }
 
+namespace {
+
+int check_common(int E, int k, int64_t T, int64_t H, int x_dtype) {
+  if (E < 1 || E > kMaxExperts) return xm_set_error(XM_ERR_INVALID, "moe: %d experts (1..%d supported)", E, kMaxExperts);
+  if (k < 1 || k > E) return xm_set_error(XM_ERR_INVALID, "moe: num_experts_per_tok=%d outside 1..%d", k, E);
+  if (T < 1 || H < 256 || H % 256) return xm_set_error(XM_ERR_INVALID, "moe: hidden size must be a positive multiple of 256");
+  if (T * k > (1 << 30)) return xm_set_error(XM_ERR_INVALID, "moe: too many tokens");
+  if (x_dtype != XM_DT_F32 && x_dtype != XM_DT_BF16 && x_dtype != XM_DT_F16)
+    return xm_set_error(XM_ERR_INVALID, "moe: bad x dtype %d", x_dtype);
+  return XM_OK;
+}
+
+// router + stable sort: topk_e/topk_w/pair_pos/sorted_tok/cnt/off in the workspace
+int route_and_sort(const void* d_x, int x_dtype, int64_t T, int64_t H, const float* d_gate, int E, int k,
+                   const MoeWs& w, cudaStream_t st) {
+  const int64_t P = T * k;
+  const unsigned tgrid = (unsigned)((T * 32 + 255) / 256);
+  if (x_dtype == XM_DT_F32)
+    k_moe_router<float><<<tgrid, 256, 0, st>>>((const float*)d_x, d_gate, (int)T, (int)H, E, k, w.topk_e, w.topk_w);
+  else if (x_dtype == XM_DT_BF16)
+    k_moe_router<__nv_bfloat16><<<tgrid, 256, 0, st>>>((const __nv_bfloat16*)d_x, d_gate, (int)T, (int)H, E, k,
+                                                         w.topk_e, w.topk_w);
+  else
+    k_moe_router<__half><<<tgrid, 256, 0, st>>>((const __half*)d_x, d_gate, (int)T, (int)H, E, k, w.topk_e, w.topk_w);
+  int rc = xm_check_launch("moe router");
+  if (rc) return rc;
+  k_moe_sort<<<1, 1024, 0, st>>>(w.topk_e, w.topk_w, (int)P, k, E, w.sorted_tok, w.sorted_w, w.pair_pos, w.cnt, w.off);
+  return xm_check_launch("moe sort");
+}
+
+// prepared fp16 rows a16 (P x H, already in expert order) -> d (P x H): the
+// SwiGLU experts of G groups (rows [off[g], off[g] + cnt[g]) use weights tab[g],
+// tab[G + g], tab[2G + g] for w1, w3, w2)
+int run_experts(const __half* a16, const float* ascale, int64_t P, int64_t H, int64_t F, const uint8_t* const* tab,
+                int G, const int* cnt, const int* off, int64_t max_rows, float* g, float* u, __half* h16,
+                float* hscale, float* d, cudaStream_t st) {
+  const int64_t expect = std::max<int64_t>(1, P / G);
+  int rc;
+  if ((rc = qgemm_q4k_grouped(a16, ascale, P, H, F, tab, cnt, off, G, max_rows, expect, g, st))) return rc;
+  if ((rc = qgemm_q4k_grouped(a16, ascale, P, H, F, tab + G, cnt, off, G, max_rows, expect, u, st))) return rc;
+  const unsigned pgrid = (unsigned)((P * 32 + 255) / 256);
+  k_swiglu_prep<<<pgrid, 256, 0, st>>>(g, u, (int)P, (int)F, h16, hscale);
+  if ((rc = xm_check_launch("moe swiglu"))) return rc;
+  return qgemm_q4k_grouped(h16, hscale, P, F, H, tab + 2 * G, cnt, off, G, max_rows, expect, d, st);
+}
+
+struct ExpertWs {
+  __half *a16, *h16;
+  float *ascale, *hscale, *g, *u;
+  int64_t bytes;
+};
+
+ExpertWs carve_experts(uint8_t* base, int64_t P, int64_t H, int64_t F) {
+  ExpertWs w{};
+  int64_t o = 0;
+  auto take = [&](int64_t bytes) { uint8_t* p = base ? base + o : nullptr; o += align256(bytes); return p; };
+  w.a16 = (__half*)take(P * H * 2);
+  w.ascale = (float*)take(P * 4);
+  w.g = (float*)take(P * F * 4);
+  w.u = (float*)take(P * F * 4);
+  w.h16 = (__half*)take(P * F * 2);
+  w.hscale = (float*)take(P * 4);
+  w.bytes = o;
+  return w;
+}
+
+}  // namespace
+
 extern "C" int xm_moe_forward(const void* d_x, int x_dtype, int64_t T, int64_t H, const float* d_gate, int E, int k,
                               int64_t F, const void* const* h_w1, const void* const* h_w3, const void* const* h_w2,
                               int qtype, float* d_out, void* d_ws, int64_t ws_bytes, void* stream) {
   if (qtype != T_Q4_K) return xm_set_error(XM_ERR_UNSUPPORTED, "moe: expert type id %d has no tensor-core path", qtype);
-  if (E < 1 || E > kMaxExperts) return xm_set_error(XM_ERR_INVALID, "moe: %d experts (1..%d supported)", E, kMaxExperts);
-  if (k < 1 || k > E) return xm_set_error(XM_ERR_INVALID, "moe: num_experts_per_tok=%d outside 1..%d", k, E);
-  if (T < 1 || H < 256 || H % 256 || F < 256 || F % 256)
+  if (int rc0 = check_common(E, k, T, H, x_dtype)) return rc0;
+  if (F < 256 || F % 256)
     return xm_set_error(XM_ERR_INVALID, "moe: hidden and intermediate sizes must be positive multiples of 256");
-  if (T * k > (1 << 30)) return xm_set_error(XM_ERR_INVALID, "moe: too many tokens");
-  if (x_dtype != XM_DT_F32 && x_dtype != XM_DT_BF16 && x_dtype != XM_DT_F16)
-    return xm_set_error(XM_ERR_INVALID, "moe: bad x dtype %d", x_dtype);
   if (!d_x || !d_gate || !d_out || !d_ws || !h_w1 || !h_w2 || !h_w3)
     return xm_set_error(XM_ERR_INVALID, "moe: null pointer");
   if (((uintptr_t)d_ws & 255) || ws_bytes < xm_moe_workspace_size(T, H, F, E, k))
@@ -291,19 +365,8 @@ extern "C" int xm_moe_forward(const void* d_x, int x_dtype, int64_t T, int64_t H
     tab[E + e] = (const uint8_t*)h_w3[e];
     tab[2 * E + e] = (const uint8_t*)h_w2[e];
   }
-
-  const unsigned tgrid = (unsigned)((T * 32 + 255) / 256);
-  if (x_dtype == XM_DT_F32)
-    k_moe_router<float><<<tgrid, 256, 0, st>>>((const float*)d_x, d_gate, (int)T, (int)H, E, k, w.topk_e, w.topk_w);
-  else if (x_dtype == XM_DT_BF16)
-    k_moe_router<__nv_bfloat16><<<tgrid, 256, 0, st>>>((const __nv_bfloat16*)d_x, d_gate, (int)T, (int)H, E, k,
-                                                         w.topk_e, w.topk_w);
-  else
-    k_moe_router<__half><<<tgrid, 256, 0, st>>>((const __half*)d_x, d_gate, (int)T, (int)H, E, k, w.topk_e, w.topk_w);
-  int rc = xm_check_launch("moe router");
+  int rc = route_and_sort(d_x, x_dtype, T, H, d_gate, E, k, w, st);
   if (rc) return rc;
-  k_moe_sort<<<1, 1024, 0, st>>>(w.topk_e, w.topk_w, (int)P, k, E, w.sorted_tok, w.sorted_w, w.pair_pos, w.cnt, w.off);
-  if ((rc = xm_check_launch("moe sort"))) return rc;
   const unsigned pgrid = (unsigned)((P * 32 + 255) / 256);
   if (x_dtype == XM_DT_F32)
     k_moe_gather_prep<float><<<pgrid, 256, 0, st>>>((const float*)d_x, w.sorted_tok, (int)P, (int)H, w.a16, w.ascale);
@@ -313,13 +376,93 @@ extern "C" int xm_moe_forward(const void* d_x, int x_dtype, int64_t T, int64_t H
   else
     k_moe_gather_prep<__half><<<pgrid, 256, 0, st>>>((const __half*)d_x, w.sorted_tok, (int)P, (int)H, w.a16, w.ascale);
   if ((rc = xm_check_launch("moe gather"))) return rc;
-
-  const int64_t expect = std::max<int64_t>(1, P / E);
-  if ((rc = qgemm_q4k_grouped(w.a16, w.ascale, P, H, F, tab, w.cnt, w.off, E, T, expect, w.g, st))) return rc;
-  if ((rc = qgemm_q4k_grouped(w.a16, w.ascale, P, H, F, tab + E, w.cnt, w.off, E, T, expect, w.u, st))) return rc;
-  k_swiglu_prep<<<pgrid, 256, 0, st>>>(w.g, w.u, (int)P, (int)F, w.h16, w.hscale);
-  if ((rc = xm_check_launch("moe swiglu"))) return rc;
-  if ((rc = qgemm_q4k_grouped(w.h16, w.hscale, P, F, H, tab + 2 * E, w.cnt, w.off, E, T, expect, w.d, st))) return rc;
+  if ((rc = run_experts(w.a16, w.ascale, P, H, F, tab, E, w.cnt, w.off, T, w.g, w.u, w.h16, w.hscale, w.d, st)))
+    return rc;
+  const unsigned tgrid = (unsigned)((T * 32 + 255) / 256);
   k_moe_combine<<<tgrid, 256, 0, st>>>(w.d, w.topk_e, w.topk_w, w.pair_pos, (int)T, (int)H, k, d_out);
+  return xm_check_launch("moe combine");
+}
+
+// ---------------------------------------------------------------------------
+// Expert parallelism: the block split at its two exchange points.
+// ---------------------------------------------------------------------------
+extern "C" int xm_moe_dispatch(const void* d_x, int x_dtype, int64_t T, int64_t H, const float* d_gate, int E, int k,
+                               int64_t F, void* d_send, int* d_cnt, void* d_ws, int64_t ws_bytes, void* stream) {
+  if (int rc = check_common(E, k, T, H, x_dtype)) return rc;
+  if (!d_x || !d_gate || !d_send || !d_cnt || !d_ws) return xm_set_error(XM_ERR_INVALID, "moe_dispatch: null pointer");
+  if (((uintptr_t)d_ws & 255) || ws_bytes < xm_moe_workspace_size(T, H, F, E, k))
+    return xm_set_error(XM_ERR_INVALID, "moe_dispatch: workspace too small or not 256-byte aligned");
+  cudaStream_t st = (cudaStream_t)stream;
+  MoeWs w = carve((uint8_t*)d_ws, T, H, F, E, k);
+  int rc = route_and_sort(d_x, x_dtype, T, H, d_gate, E, k, w, st);
+  if (rc) return rc;
+  const int64_t P = T * k;
+  const dim3 grid((unsigned)std::min<int64_t>((H + 255) / 256, 8), (unsigned)P);
+  if (x_dtype == XM_DT_F32)
+    k_moe_gather<float><<<grid, 256, 0, st>>>((const float*)d_x, w.sorted_tok, (int)P, (int)H, (float*)d_send);
+  else if (x_dtype == XM_DT_BF16)
+    k_moe_gather<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)d_x, w.sorted_tok, (int)P, (int)H,
+                                                       (__nv_bfloat16*)d_send);
+  else
+    k_moe_gather<__half><<<grid, 256, 0, st>>>((const __half*)d_x, w.sorted_tok, (int)P, (int)H, (__half*)d_send);
+  if ((rc = xm_check_launch("moe gather"))) return rc;
+  cudaError_t e = cudaMemcpyAsync(d_cnt, w.cnt, E * sizeof(int), cudaMemcpyDeviceToDevice, st);
+  if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "moe_dispatch: %s", cudaGetErrorString(e));
+  return XM_OK;
+}
+
+extern "C" int64_t xm_moe_experts_workspace_size(int64_t P, int64_t H, int64_t F) {
+  if (P < 1 || H < 1 || F < 1) return 0;
+  return carve_experts(nullptr, P, H, F).bytes;
+}
+
+extern "C" int xm_moe_experts(const void* d_rows, int x_dtype, int64_t P, int64_t H, int64_t F, int G, const int* d_cnt,
+                              const int* d_off, const void* const* h_w1, const void* const* h_w3,
+                              const void* const* h_w2, int qtype, int64_t max_rows, float* d_out, void* d_ws,
+                              int64_t ws_bytes, void* stream) {
+  if (qtype != T_Q4_K) return xm_set_error(XM_ERR_UNSUPPORTED, "moe_experts: expert type id %d has no tensor-core path", qtype);
+  if (G < 1 || G > kMaxExperts) return xm_set_error(XM_ERR_INVALID, "moe_experts: %d groups (1..%d)", G, kMaxExperts);
+  if (P < 0 || H < 256 || H % 256 || F < 256 || F % 256 || max_rows < 0)
+    return xm_set_error(XM_ERR_INVALID, "moe_experts: bad sizes");
+  if (x_dtype != XM_DT_F32 && x_dtype != XM_DT_BF16 && x_dtype != XM_DT_F16)
+    return xm_set_error(XM_ERR_INVALID, "moe_experts: bad x dtype %d", x_dtype);
+  if (P == 0) return XM_OK;
+  if (!d_rows || !d_cnt || !d_off || !d_out || !d_ws || !h_w1 || !h_w2 || !h_w3)
+    return xm_set_error(XM_ERR_INVALID, "moe_experts: null pointer");
+  if (((uintptr_t)d_ws & 255) || ws_bytes < xm_moe_experts_workspace_size(P, H, F))
+    return xm_set_error(XM_ERR_INVALID, "moe_experts: workspace too small or not 256-byte aligned");
+  const uint8_t* tab[3 * kMaxExperts];
+  for (int g = 0; g < G; ++g) {
+    if (!h_w1[g] || !h_w2[g] || !h_w3[g] || ((uintptr_t)h_w1[g] & 15) || ((uintptr_t)h_w2[g] & 15) ||
+        ((uintptr_t)h_w3[g] & 15))
+      return xm_set_error(XM_ERR_INVALID, "moe_experts: group %d weight pointer null or not 16-byte aligned", g);
+    tab[g] = (const uint8_t*)h_w1[g];
+    tab[G + g] = (const uint8_t*)h_w3[g];
+    tab[2 * G + g] = (const uint8_t*)h_w2[g];
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  ExpertWs w = carve_experts((uint8_t*)d_ws, P, H, F);
+  const unsigned pgrid = (unsigned)((P * 32 + 255) / 256);
+  if (x_dtype == XM_DT_F32)
+    k_moe_gather_prep<float><<<pgrid, 256, 0, st>>>((const float*)d_rows, nullptr, (int)P, (int)H, w.a16, w.ascale);
+  else if (x_dtype == XM_DT_BF16)
+    k_moe_gather_prep<__nv_bfloat16><<<pgrid, 256, 0, st>>>((const __nv_bfloat16*)d_rows, nullptr, (int)P, (int)H,
+                                                              w.a16, w.ascale);
+  else
+    k_moe_gather_prep<__half><<<pgrid, 256, 0, st>>>((const __half*)d_rows, nullptr, (int)P, (int)H, w.a16, w.ascale);
+  int rc = xm_check_launch("moe_experts prep");
+  if (rc) return rc;
+  return run_experts(w.a16, w.ascale, P, H, F, tab, G, d_cnt, d_off, std::max<int64_t>(1, max_rows), w.g, w.u, w.h16,
+                     w.hscale, d_out, st);
+}
+
+extern "C" int xm_moe_combine(const float* d_rows, int64_t T, int64_t H, int E, int k, int64_t F, const void* d_ws,
+                              float* d_out, void* stream) {
+  if (int rc = check_common(E, k, T, H, XM_DT_F32)) return rc;
+  if (!d_rows || !d_ws || !d_out) return xm_set_error(XM_ERR_INVALID, "moe_combine: null pointer");
+  MoeWs w = carve((uint8_t*)d_ws, T, H, F, E, k);
+  const unsigned tgrid = (unsigned)((T * 32 + 255) / 256);
+  k_moe_combine<<<tgrid, 256, 0, (cudaStream_t)stream>>>(d_rows, w.topk_e, w.topk_w, w.pair_pos, (int)T, (int)H, k,
+                                                          d_out);
   return xm_check_launch("moe combine");
 }

@@ -92,4 +92,96 @@ class MoELayer:
         return f"<MoELayer experts={self.num_experts} {mode} activation={self.activation}>"
 
 
-__all__ = ["MoELayer"]
+class MoELayerEP:
+    """Expert-parallel MoE block: ``world`` ranks (one process per GPU) each
+    hold E / world experts (rank r owns experts r*E/world .. (r+1)*E/world - 1)
+    and route their own tokens.  ``forward_device(x)`` on every rank: route and
+    sort the local tokens (``xm_moe_dispatch``), exchange the per-expert counts
+    and then the selected rows with ``all_to_all`` over the process group
+    (NCCL), run the local experts on the received rows as (source rank, local
+    expert) groups of the tensor-core grouped GEMM (``xm_moe_experts``),
+    exchange the result rows back and combine them in ascending expert order
+    (``xm_moe_combine``).  The result equals the single-GPU ``MoELayer`` on the
+    same weights.  ``weights`` is the reference's nested dict; only the local
+    experts' entries are read."""
+
+    def __init__(self, config, weights, rank: int, world: int, process_group=None):
+        import torch.distributed as dist
+        self.num_experts = E = config["num_experts"]
+        self.num_experts_per_tok = k = config["num_experts_per_tok"]
+        if k < 1 or k > E:
+            raise ValueError(f"MoELayerEP: num_experts_per_tok={k} outside 1..{E}")
+        if E % world:
+            raise ValueError(f"MoELayerEP: {E} experts do not divide over {world} ranks")
+        if config.get("hidden_act", "silu") not in ("silu", "swish"):
+            raise NotImplementedError("MoELayerEP supports silu experts")
+        self.rank, self.world = rank, world
+        self.pg = process_group if process_group is not None else dist.group.WORLD
+        self.e_local = E // world
+        gate_w = weights["gate"]["weight"]
+        gate_w = gate_w if isinstance(gate_w, torch.Tensor) else torch.as_tensor(np.asarray(gate_w, np.float32))
+        self.w1, self.w2, self.w3 = [], [], []
+        for i in range(rank * self.e_local, (rank + 1) * self.e_local):
+            exp = weights["experts"][str(i)]
+            for name, dst in (("w1", self.w1), ("w2", self.w2), ("w3", self.w3)):
+                w = exp[name]["weight"]
+                if not isinstance(w, GGUFTensor):
+                    raise TypeError("expert weights must be GGUFTensor (quantized blocks resident on the GPU)")
+                dst.append(w)
+        self.device = self.w1[0].device
+        self.gate = gate_w.to(device=self.device, dtype=torch.float32).contiguous()
+        self.hidden = self.gate.shape[1]
+        self.intermediate = self.w1[0].shape[0]
+        self.qtype = self.w1[0].qtype.type_id
+        # group g = (source rank s, local expert e) -> expert e's weights
+        G = world * self.e_local
+        self._p1 = (ctypes.c_void_p * G)(*[self.w1[g % self.e_local].data.data_ptr() for g in range(G)])
+        self._p3 = (ctypes.c_void_p * G)(*[self.w3[g % self.e_local].data.data_ptr() for g in range(G)])
+        self._p2 = (ctypes.c_void_p * G)(*[self.w2[g % self.e_local].data.data_ptr() for g in range(G)])
+
+    def forward_device(self, x: torch.Tensor) -> torch.Tensor:
+        """x: this rank's tokens, CUDA (..., H) -> fp32 CUDA tensor of the same shape."""
+        import torch.distributed as dist
+        H, F, E, k = self.hidden, self.intermediate, self.num_experts, self.num_experts_per_tok
+        W, El = self.world, self.e_local
+        if x.shape[-1] != H:
+            raise ValueError(f"x has {x.shape[-1]} features, the router expects {H}")
+        if x.dtype not in _DT:
+            x = x.float()
+        xf = x.reshape(-1, H).contiguous()
+        T = xf.shape[0]
+        dev = x.device
+        st = torch.cuda.current_stream(dev).cuda_stream
+        ws = _workspace(dev, lib.xm_moe_workspace_size(T, H, F, E, k))
+        send = torch.empty((T * k, H), dtype=xf.dtype, device=dev)
+        cnt = torch.empty(E, dtype=torch.int32, device=dev)
+        with torch.cuda.device(dev):
+            check(lib.xm_moe_dispatch(xf.data_ptr(), _DT[xf.dtype], T, H, self.gate.data_ptr(), E, k, F,
+                                      send.data_ptr(), cnt.data_ptr(), ws.data_ptr(), ws.numel(), st), "moe_dispatch")
+            recv_cnt = torch.empty(E, dtype=torch.int32, device=dev)   # [source rank][local expert]
+            dist.all_to_all_single(recv_cnt, cnt, group=self.pg)
+            c_send = cnt.view(W, El).sum(1).cpu().tolist()
+            rc = recv_cnt.cpu()
+            c_recv = rc.view(W, El).sum(1).tolist()
+            R = int(sum(c_recv))
+            recv = torch.empty((R, H), dtype=xf.dtype, device=dev)
+            dist.all_to_all_single(recv, send, c_recv, c_send, group=self.pg)
+            off = torch.cumsum(rc, 0) - rc
+            g_cnt = rc.to(dev)
+            g_off = off.to(torch.int32).to(dev)
+            rows = torch.empty((R, H), dtype=torch.float32, device=dev)
+            if R:
+                ews = torch.empty(lib.xm_moe_experts_workspace_size(R, H, F), dtype=torch.uint8, device=dev)
+                check(lib.xm_moe_experts(recv.data_ptr(), _DT[xf.dtype], R, H, F, W * El, g_cnt.data_ptr(),
+                                         g_off.data_ptr(), self._p1, self._p3, self._p2, self.qtype,
+                                         int(rc.max()), rows.data_ptr(), ews.data_ptr(), ews.numel(), st),
+                      "moe_experts")
+            back = torch.empty((T * k, H), dtype=torch.float32, device=dev)
+            dist.all_to_all_single(back, rows, c_send, c_recv, group=self.pg)
+            out = torch.empty((T, H), dtype=torch.float32, device=dev)
+            check(lib.xm_moe_combine(back.data_ptr(), T, H, E, k, F, ws.data_ptr(), out.data_ptr(), st),
+                  "moe_combine")
+        return out.reshape(x.shape)
+
+
+__all__ = ["MoELayer", "MoELayerEP"]
