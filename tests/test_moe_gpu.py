@@ -101,7 +101,8 @@ def test_split_entry_points_match_fused(T, E, k, H, F, shards):
     p2 = (ctypes.c_void_p * G)(*[layer.w2[g].data.data_ptr() for g in range(G)])
     rows = torch.empty(T * k, H, dtype=torch.float32, device="cuda")
     ews = torch.empty(lib.xm_moe_experts_workspace_size(T * k, H, F), dtype=torch.uint8, device="cuda")
-    check(lib.xm_moe_experts(send.data_ptr(), DT_BF16, T * k, H, F, G, c.cuda().data_ptr(), off.cuda().data_ptr(),
+    c_dev, off_dev = c.cuda(), off.cuda()          # kept alive: the kernels read them after the call returns
+    check(lib.xm_moe_experts(send.data_ptr(), DT_BF16, T * k, H, F, G, c_dev.data_ptr(), off_dev.data_ptr(),
                              p1, p3, p2, 12, int(c.max()), rows.data_ptr(), ews.data_ptr(), ews.numel(), st), "experts")
     out = torch.empty(T, H, dtype=torch.float32, device="cuda")
     check(lib.xm_moe_combine(rows.data_ptr(), T, H, E, k, F, ws.data_ptr(), out.data_ptr(), st), "combine")
