@@ -133,3 +133,31 @@ def test_prologue_needs_integer_path():
     with pytest.raises(NotImplementedError):
         qgemv_ex(W, x, 1, 256, PRO_RMSNORM, torch.ones(256, device="cuda"))
     assert lib.xm_device_status(1) == 0
+
+
+@pytest.mark.parametrize("n,k", [(4096, 4096), (6144, 4096), (1000, 2048), (37, 512), (28672, 4096), (300, 8192)])
+@pytest.mark.parametrize("m", [2, 3, 4, 5, 8])
+def test_q4k_tensor_core_batch(n, k, m):
+    """Q4_K with 2..8 activation rows runs on the tensor cores (integer MMA,
+    one scale per activation row); plain, RMSNorm prologue and residual add."""
+    raw, wf = weight("Q4_K", n, k, 51)
+    rng = np.random.default_rng(52)
+    x = (2.0 * rng.standard_normal((m, k))).astype(np.float32)
+    W = GGUFTensor(raw, "Q4_K", (n, k))
+    y = qlinear(W, torch.from_numpy(x).cuda()).cpu().numpy()
+    assert rel_err(y, x @ wf.T) < GEMV_TOL
+    nw = (1.0 + 0.1 * rng.standard_normal(k)).astype(np.float32)
+    h0 = rng.standard_normal((m, n)).astype(np.float32)
+    yy = torch.from_numpy(h0.copy()).cuda()
+    qgemv_ex(W, torch.from_numpy(x).cuda(), m, k, PRO_RMSNORM, torch.from_numpy(nw).cuda(), y=yy, accumulate=True)
+    assert rel_err(yy.cpu().numpy(), h0 + rms(x, nw) @ wf.T) < GEMV_TOL
+    assert lib.xm_device_status(0) == 0
+
+
+def test_q4k_tensor_core_swiglu():
+    raw, wf = weight("Q4_K", 2048, 4096, 53)
+    rng = np.random.default_rng(54)
+    gu = (2.0 * rng.standard_normal((6, 8192))).astype(np.float32)
+    y = qgemv_ex(GGUFTensor(raw, "Q4_K", (2048, 4096)), torch.from_numpy(gu).cuda(), 6, 8192, PRO_SWIGLU)
+    ref = (silu(gu[:, :4096]) * gu[:, 4096:]) @ wf.T
+    assert rel_err(y.cpu().numpy(), ref) < GEMV_TOL

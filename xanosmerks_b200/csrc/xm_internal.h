@@ -22,3 +22,11 @@ int gemv_kq(int qtype, const uint8_t* W, int64_t n, int64_t k, int64_t m, const 
 // Group-major activation split of m rows of k values with an XM_PRO_* prologue.
 int split_rows(const void* d_x, int x_dtype, int64_t m, int64_t k, int64_t x_stride, int prologue,
                const float* norm_w, float eps, void* d_ws, cudaStream_t st);
+// Q4_K GEMV for 2..8 activation rows on the tensor cores (integer MMA): the
+// per-row activation split (with an XM_PRO_* prologue) goes to d_ws, which must
+// hold gemv_mma_split_bytes(k, m) bytes; y (+)= W x (+ bias).
+bool gemv_mma_supported(int qtype, int64_t n, int64_t k, int64_t m);
+int64_t gemv_mma_split_bytes(int64_t k, int64_t m);
+int gemv_mma(const uint8_t* W, int64_t n, int64_t k, int64_t m, const void* d_x, int x_dtype, int64_t x_stride,
+             int prologue, const float* norm_w, float eps, const float* bias, float* y, int accumulate, void* d_ws,
+             cudaStream_t st);

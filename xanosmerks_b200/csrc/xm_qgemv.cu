@@ -1005,6 +1005,9 @@ extern "C" int xm_qgemv(int qtype, const void* d_w, int64_t w_bytes, int64_t n, 
     return k4096_fused(x_dtype, W, n, d_x, nullptr, 0.f, d_bias, d_y, 0, st);
   const bool ws_ok =
       d_workspace && workspace_bytes >= xm_qgemv_workspace_size(k, m) && aligned16(d_workspace);
+  if (ws_ok && aligned16(d_w) && m >= 2 && gemv_mma_supported(qtype, n, k, m) &&
+      workspace_bytes >= gemv_mma_split_bytes(k, m))
+    return gemv_mma(W, n, k, m, d_x, x_dtype, k, XM_PRO_NONE, nullptr, 0.f, d_bias, d_y, 0, d_workspace, st);
   if (ws_ok && aligned16(d_w) && integer_path(qtype, n, k, m)) {
     rc = split_activation(d_x, x_dtype, m, k, d_workspace, st);
     if (rc) return rc;
@@ -1037,6 +1040,10 @@ extern "C" int xm_qgemv_ex(int qtype, const void* d_w, int64_t w_bytes, int64_t 
                        accumulate, st);
   const bool ws_ok =
       d_workspace && workspace_bytes >= xm_qgemv_workspace_size(k, m) && aligned16(d_workspace);
+  if (ws_ok && aligned16(d_w) && m >= 2 && gemv_mma_supported(qtype, n, k, m) &&
+      workspace_bytes >= gemv_mma_split_bytes(k, m))
+    return gemv_mma(W, n, k, m, d_x, x_dtype, x_stride, prologue, d_norm_w, eps, d_bias, d_y, accumulate,
+                    d_workspace, st);
   if (ws_ok && aligned16(d_w) && integer_path(qtype, n, k, m)) {
     rc = split_rows(d_x, x_dtype, m, k, x_stride, prologue, d_norm_w, eps, d_workspace, st);
     if (rc) return rc;
