@@ -45,7 +45,7 @@ METRIC = "Q4_K GEMV weight GB/s"
 UNIT = "GB/s"
 # DRAM bytes read+written per launch of the GEMV kernel on this shape, from the
 # ncu capture summarised in profiles/q4k_gemv_k4096_m1_11008x4096.md.
-NCU_TRAFFIC_PER_LAUNCH = 25_398_784
+NCU_TRAFFIC_PER_LAUNCH = 25_409_536
 KERNEL = "k_qgemv_q4k_k4096_m1<bf16> (fused activation split)"
 
 
@@ -62,6 +62,10 @@ def parse():
     ap.add_argument("--no-decode", action="store_true", help="skip the Llama decode tok/s section")
     ap.add_argument("--no-moe", action="store_true", help="skip the MoE block section")
     ap.add_argument("--decode-steps", type=int, default=64)
+    ap.add_argument("--decode-profile", type=int, default=0,
+                    help="profiling mode: two graph-replayed decode steps of this batch size between "
+                         "cudaProfilerStart/Stop (with --decode-layers layers)")
+    ap.add_argument("--decode-layers", type=int, default=2)
     ap.add_argument("--gemm-m", type=int, default=0,
                     help="only time the prefill GEMM with this many activation rows (profiling mode)")
     return ap.parse_args()
@@ -540,6 +544,29 @@ def run_gemm_only(args):
                       "TFLOPS": round(2.0 * mm * N * K / us / 1e6, 1), "clocks": clk.summary()}), flush=True)
 
 
+def run_decode_profile(args):
+    """Profiling mode: the bench's Llama shapes with --decode-layers layers, an
+    8-token prompt, one eager decode step, then two replays of the captured
+    step between cudaProfilerStart and cudaProfilerStop."""
+    import torch
+    from xanosmerks_b200.llama import LlamaConfig, LlamaDecoder, LlamaWeights, synth_llama_weights
+    B = args.decode_profile
+    cfg = LlamaConfig(num_layers=args.decode_layers)
+    w = LlamaWeights.from_full(cfg, synth_llama_weights(cfg, seed=0, device="cuda"))
+    dec = LlamaDecoder(w, batch=B, max_ctx=640)
+    ids = np.random.default_rng(0).integers(0, cfg.vocab_size, size=(B, 8))
+    dec.prefill(torch.from_numpy(ids))
+    dec.decode_step()
+    dec.length += 1
+    dec.capture()
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStart()
+    dec.replay(2)
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
+    print(json.dumps({"decode_profile": B, "layers": args.decode_layers, "ok": True}), flush=True)
+
+
 def moe_case(dev, T=1024, E=8, k=2, H=4096, F=14336, seed=0):
     """Mixtral-shape MoE block with random-init Q4_K experts (seeded)."""
     import torch
@@ -584,6 +611,9 @@ def main():
     args = parse()
     if args.moe:
         run_moe_only(args)
+        return
+    if args.decode_profile:
+        run_decode_profile(args)
         return
     if args.gemm_m:
         run_gemm_only(args)

@@ -341,7 +341,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_qgemv_q4k_tma(const uint8_t
 // Q4_K GEMV for one activation row and K = 4096 (16 super-blocks per row):
 // the decode shape of every Q4_K projection of the Llama-7B-class layer.
 //
-// Warp-specialised.  A producer warp streams the CTA's rows into an 11-slot
+// Warp-specialised.  A producer warp streams the CTA's rows into a 20-slot
 // shared-memory ring, four rows (9,216 B) per cp.async.bulk (TMA without
 // multicast; copies this large keep HBM busy, 2 KB copies do not), refilling
 // a slot as soon as its rows have been taken (full/empty mbarrier pair per
@@ -357,14 +357,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_qgemv_q4k_tma(const uint8_t
 // ---------------------------------------------------------------------------
 constexpr int kWsConsumers = 15;   // + the producer: 16 warps, so the register budget is 128 per thread
 constexpr int kWsThreads = (kWsConsumers + 1) * 32;
-constexpr int kWsSlots = 11;
+// 20 slots (184 KB): a CTA's whole share of an 11008 x 4096 matrix (75 rows,
+// 171 KB) is in flight before the consumers finish their activation prologue
+constexpr int kWsSlots = 20;
 constexpr int kWsRowsPerSlot = 4;
 constexpr int kRowBytes4096 = 16 * 144;
 constexpr int kWsSlotBytes = kWsRowsPerSlot * kRowBytes4096;
 // slots | lane-major split | barriers and counters | (fused form) the raw fp32/bf16 row of x
-// (barriers 23 x 8 B + counter + 11 slot tags = 232 B, rounded up so that the
+// (barriers 41 x 8 B + counter + 20 slot tags = 412 B, rounded up so that the
 // row of x behind it keeps the 16-byte alignment a bulk copy needs)
-constexpr int kWsCtlBytes = 256;
+constexpr int kWsCtlBytes = 512;
 static_assert((2 * kWsSlots + 1) * 8 + (kWsSlots + 1) * 4 <= kWsCtlBytes, "control block");
 static_assert((kWsSlots * kWsSlotBytes + kLaneMajorBytes + kWsCtlBytes) % 16 == 0, "x row alignment");
 // + 64 B behind the row of x for the RMSNorm partial sums
