@@ -13,18 +13,20 @@
 // fp32 `x @ W.T` only in summation order (and, for fp32 x, in x's fp16
 // rounding).
 //
-// Structure (one CTA per output tile of MT*128 rows x BN columns):
+// Two kernels:
+//  * k_qgemm_q4k_pair (the default): persistent CTA pairs on tcgen05
+//    cta_group::2 (M = 256 per MMA), raw Q4_K records staged by TMA and decoded
+//    by two interleaved groups of decode warps, double-buffered TMEM
+//    accumulators with dedicated epilogue warps; dense and grouped (MoE)
+//    modes.  Its own comment block below has the details.
+//  * k_qgemm_q4k_tc: one CTA per output tile of MT*128 rows x BN columns, used
+//    when a device cannot hold a CTA pair of the chosen size:
 //   warp 0      TMA producer of the activation tiles (fp16, 128-byte swizzle,
 //               2-D tensor map, no multicast).
 //   warp 1      allocates tensor memory and issues tcgen05.mma (one thread).
 //   warps 2-17  decode the weight blocks into the fp16 B tile of each
 //               64-wide K step, written straight into the UMMA K-major
-//               128-byte-swizzled layout.  The blocks are read from global
-//               memory (the whole quantized matrix stays L2-resident across
-//               the M tiles) one K step ahead into registers; one thread
-//               decodes one 32-weight sub-block of one row per item with
-//               packed fp32x2 arithmetic.  Afterwards these warps run the
-//               epilogue (tcgen05.ld -> row scale -> y).
+//               128-byte-swizzled layout, then run the epilogue.
 // Pipelines are mbarrier rings with bounded waits.
 #include <cuda.h>
 
@@ -189,21 +191,24 @@ XM_DEV RawItem load_item(const uint8_t* W, int64_t row_bytes, int n, int N, int 
   return it;
 }
 
-// Decode one item into fp16 and store its 4 chunks into the swizzled B row.
-XM_DEV void decode_item(const RawItem& it, int h, int j, uint8_t* row, int n) {
-  const uint32_t A = it.hd.y, B = it.hd.z, C = it.hd.w;
+// Decode chunks c0 .. c0+NC-1 (8 weights each) of sub-block 2j+h of one row
+// into fp16 and store them into the swizzled B row (n: the row's index within
+// its 8-row swizzle group pattern).  qw holds the qs words of those chunks,
+// two per chunk; hd is the record's 16-byte header.
+template <int NC>
+XM_DEV void decode_part(const uint4& hd, const uint32_t (&qw)[2 * NC], int h, int j, int c0, uint8_t* row, int n) {
+  const uint32_t A = hd.y, B = hd.z, C = hd.w;
   const int sub = 2 * j + h;
   const uint32_t scw = sub < 4 ? (A & 0x3F3F3F3Fu) : ((C & 0x0F0F0F0Fu) | ((A >> 2) & 0x30303030u));
   const uint32_t mnw = sub < 4 ? (B & 0x3F3F3F3Fu) : (((C >> 4) & 0x0F0F0F0Fu) | ((B >> 2) & 0x30303030u));
-  const float d = __half2float(__ushort_as_half((unsigned short)(it.hd.x & 0xFFFF)));
-  const float dmin = __half2float(__ushort_as_half((unsigned short)(it.hd.x >> 16)));
+  const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFF)));
+  const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
   const float d1 = __fmul_rn(d, byte_f(scw, sub & 3));       // exact (11-bit x 6-bit)
   const float m1 = __fmul_rn(dmin, byte_f(mnw, sub & 3));
   const float2 dd = make_float2(d1, d1), mm = make_float2(-m1, -m1), mg = make_float2(-8388608.0f, -8388608.0f);
-  const uint32_t qw[8] = {it.q0.x, it.q0.y, it.q0.z, it.q0.w, it.q1.x, it.q1.y, it.q1.z, it.q1.w};
   const int sh = 4 * h;
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {           // chunk c: weights 8c .. 8c+7 of the sub-block
+  for (int c = 0; c < NC; ++c) {          // chunk c0 + c: weights 8(c0+c) .. 8(c0+c)+7 of the sub-block
     uint32_t hv[4];
 #pragma unroll
     for (int wv = 0; wv < 2; ++wv) {
@@ -220,9 +225,15 @@ XM_DEV void decode_item(const RawItem& it, int h, int j, uint8_t* row, int n) {
         hv[2 * wv + p] = *reinterpret_cast<const uint32_t*>(&hh);
       }
     }
-    const int chunk = 4 * h + c;
+    const int chunk = 4 * h + c0 + c;
     *reinterpret_cast<uint4*>(row + ((chunk ^ (n & 7)) << 4)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
   }
+}
+
+// One whole item (all 4 chunks of the sub-block).
+XM_DEV void decode_item(const RawItem& it, int h, int j, uint8_t* row, int n) {
+  const uint32_t qw[8] = {it.q0.x, it.q0.y, it.q0.z, it.q0.w, it.q1.x, it.q1.y, it.q1.z, it.q1.w};
+  decode_part<4>(it.hd, qw, h, j, 0, row, n);
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -381,6 +392,394 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Persistent CTA-pair GEMM (prefill and MoE expert GEMMs).
+//
+// A cluster of two CTAs on neighbouring SMs computes 256-row output tiles
+// with tcgen05.mma.cta_group::2 (M = 256): CTA r of the pair holds activation
+// rows [128r, 128r+128) of the tile and decodes its half of every N = BN
+// weight block (output columns [r*BN/2, (r+1)*BN/2) of that block), so each
+// SM decodes half of the B operand that the 256-row MMA consumes and reads
+// only its own halves from shared memory.  Tiles go round-robin over the
+// pairs (order: pair_tile).
+//
+// Per CTA (2 + 16 + 4 warps):
+//   warp 0      TMA producer: raw Q4_K records of the CTA's weight rows, one
+//               256-wide super-block column per stage (box 144 B x BN/2 rows,
+//               per N half), and the fp16 activation box (64 K x 128 rows,
+//               128-byte swizzle) of every 64-wide K step.  Rank 1's
+//               activation box completes on rank 0's barrier (cta_group::2
+//               form of the tensor load; no multicast).
+//   warp 1      TMEM allocation (both ranks); rank 0 issues the MMAs.
+//   warps 2-17  decode, two groups of 8 warps taking turns by K step: one
+//               thread per (row, 32-weight sub-block) item, from the staged
+//               records into the swizzled B half of its CTA.
+//   warps 18-21 epilogue: TMEM -> row scale (+ bias) -> y, one TMEM
+//               sub-partition each, while the MMA fills the other accumulator.
+// Every per-step loop keeps its ring position and phase in running counters:
+// those loops run on single threads, where an integer division per step
+// costs more than the step's synchronisation.
+//
+// Barriers (all waits bounded; a timeout sets the device error word and later
+// waits give up at once, so a lost arrival ends the kernel instead of hanging):
+//   wfull/wempty[RW]   raw record ring (TMA bytes / 16 decode-warp arrivals)
+//   ofull[S]           (rank 0 only) operand stage of both CTAs: the two
+//                      producers' expect-tx arrivals and TMA bytes + the 8 + 8
+//                      warps of the decode group that owns the step
+//   oempty[S]          MMA commit, multicast to both CTAs
+//   acc_full[2]        MMA commit after the tile's last K step, both CTAs
+//   acc_empty[2]       (rank 0) 4 + 4 epilogue warps of the two CTAs
+// Remote arrivals use the default (release, CTA-scope) semantics: a
+// cluster-scope release costs ~200 ns per arrival here against ~50 ns.
+// ---------------------------------------------------------------------------
+constexpr int kPairEpiWarps = 4;
+constexpr int pair_threads(int dw) { return (2 + dw + kPairEpiWarps) * 32; }
+constexpr int kMaxRawStages = 2;
+constexpr int kRecBytes = 144;                 // one Q4_K super-block record
+constexpr int kEpiTileFloats = 32 * 33;        // per-warp padded 32 x 32 staging tile
+
+struct PairSmem {
+  uint64_t wfull[kMaxRawStages], wempty[kMaxRawStages];
+  uint64_t ofull[kMaxStages], oempty[kMaxStages];
+  uint64_t acc_full[2], acc_empty[2];
+  uint32_t tmem_base;
+};
+
+XM_DEV uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cta address -> shared::cluster address of the same variable in CTA `rank`
+XM_DEV uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+XM_DEV void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+XM_DEV void mbar_arrive_expect_tx_remote(uint32_t cluster_addr, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cluster.b64 _, [%0], %1;" ::"r"(cluster_addr), "r"(bytes)
+               : "memory");
+}
+XM_DEV bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+               : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Bounded wait.  A non-blocking test first: most waits find the phase already
+// complete, and try_wait costs noticeably more than test_wait even then.
+// Gives up at once when another wait anywhere has recorded a timeout.
+// Barriers that count arrivals from the peer CTA are waited on with the
+// default (CTA-scope) acquire, as in the established 2-SM MMA pipelines: the
+// peer's arrivals follow its proxy fence, and the mbarrier phase completion
+// orders them before the MMAs issued after tcgen05.fence::after_thread_sync.
+XM_DEV bool pair_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_test_wait(bar, parity)) return true;
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u && *reinterpret_cast<volatile int*>(&g_xm_device_error)) return false;
+  }
+  atomicOr(&g_xm_device_error, XM_DEVERR_TIMEOUT);
+  return false;
+}
+// 2-D tensor load into this CTA's shared memory whose completion is counted
+// on an mbarrier of either CTA of the pair (no multicast)
+XM_DEV void tma_load_2d_pair(void* dst, const CUtensorMap* map, int c0, int c1, uint32_t bar_cluster_addr) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(c0), "r"(c1), "r"(bar_cluster_addr)
+      : "memory");
+}
+XM_DEV void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+XM_DEV void tc2_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// arrive on `bar` (same shared offset) in both CTAs of the pair once the
+// previously issued MMAs have completed
+XM_DEV void tc2_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+      ::"r"(smem_u32(bar)), "h"((uint16_t)3)
+      : "memory");
+}
+__host__ __device__ constexpr uint32_t idesc_f16_f32_m256(int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+}
+
+// Weight tensor maps and (grouped mode) the device-side row ranges of the
+// groups.  NMAP = 1: one dense GEMM; NMAP = kMaxGroups: group g multiplies
+// activation rows [off[g], off[g] + cnt[g]) with weight g.
+template <int NMAP>
+struct PairW {
+  CUtensorMap map[NMAP];
+  const int* cnt;
+  const int* off;
+  int groups;
+};
+
+struct PairTile {
+  int g, am0, mhi, col0;   // group, first activation row of the 256-row tile, row limit, first output column
+};
+
+// Tile t of the round-robin order.  Dense: m-fastest, so the pairs that run
+// together share a weight column tile in L2.  Grouped: n-fastest within
+// (group, m tile), so the tiles past a group's row count (skipped, identically
+// by every role) form whole runs and the real tiles spread evenly over pairs.
+template <int NMAP>
+XM_DEV bool pair_tile(const PairW<NMAP>& pw, int t, int M, int TM, int TN, int width, PairTile& pt) {
+  if (NMAP == 1) {
+    pt.g = 0;
+    pt.am0 = (t % TM) * 256;
+    pt.mhi = M;
+    pt.col0 = (t / TM) * width;
+    return true;
+  }
+  const int nt = t % TN, r = t / TN;
+  const int mt = r % TM, g = r / TM;
+  const int lo = pw.off[g], cnt = pw.cnt[g];
+  pt.g = g;
+  pt.am0 = lo + mt * 256;
+  pt.mhi = lo + cnt;
+  pt.col0 = nt * width;
+  return mt * 256 < cnt;
+}
+
+// NH = 1: tile 256 x BN, two accumulators (the epilogue of one tile overlaps
+// the main loop of the next).  NH = 2: tile 256 x 2BN as two N = BN MMAs into
+// one accumulator of 2BN columns (fewer, wider tiles for mid-size M).
+template <int DW, int NMAP>
+__global__ void __launch_bounds__(pair_threads(DW), 1)
+    k_qgemm_q4k_pair(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ PairW<NMAP> pw, int M,
+                     int N, int K, int BN, int NH, int S, int RW, int TM, const float* __restrict__ rowscale,
+                     const float* __restrict__ bias, float* __restrict__ y) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int hb = BN >> 1;                         // rows of each N half this CTA decodes
+  const int rows = NH * hb;                       // weight rows decoded by this CTA per K step
+  const int width = NH * BN;                      // output columns of a tile
+  const int ostage = kATileBytes + rows * 128;    // [A 128 x 64 fp16 | B half 0 | B half 1], 1024-byte multiples
+  const int wstage = rows * kRecBytes;            // the CTA's records of one super-block column
+  uint8_t* sO = base;
+  uint8_t* sW = sO + S * ostage;
+  float* sEpi = reinterpret_cast<float*>(sW + RW * wstage);
+  PairSmem* ctl = reinterpret_cast<PairSmem*>(sEpi + kPairEpiWarps * kEpiTileFloats);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int TN = (N + width - 1) / width;
+  const int T = TM * TN * (NMAP == 1 ? 1 : pw.groups);
+  const int KB = K >> 8, nkt = K / kBK;
+  const int nacc = NH == 1 ? 2 : 1;               // accumulators of `width` columns in TMEM
+
+  if (tid == 0) {
+    for (int i = 0; i < RW; ++i) {
+      mbar_init(&ctl->wfull[i], 1);
+      mbar_init(&ctl->wempty[i], DW);
+    }
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&ctl->ofull[i], 2 + 2 * 8);       // rank 0 only: 2 producers + 8 warps of one decode group per CTA
+      mbar_init(&ctl->oempty[i], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&ctl->acc_full[b], 1);
+      mbar_init(&ctl->acc_empty[b], 2 * kPairEpiWarps);
+    }
+    fence_mbar_init();
+  }
+  constexpr uint32_t kCols = 512;                 // nacc * width <= 512 columns
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&ctl->tmem_base)),
+                 "r"(kCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();                             // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  // the group row ranges (and the prepared activation) come from the preceding kernel
+  if (NMAP > 1) grid_dep_wait();
+
+  // Ring positions advance incrementally (no division on the per-step paths,
+  // which run on single threads).  Waits on an "empty" barrier use the
+  // opposite parity, so the first lap passes at once.
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      grid_dep_wait();
+      const uint32_t leader_ofull = mapa_shared(smem_u32(&ctl->ofull[0]), 0);
+      uint32_t s = 0, ph = 0, rs = 0, rph = 0;
+      for (int t = pair; t < T; t += npairs) {
+        PairTile pt;
+        if (!pair_tile(pw, t, M, TM, TN, width, pt)) continue;
+        const CUtensorMap* wmap = &pw.map[NMAP == 1 ? 0 : pt.g];
+        const int am = pt.am0 + (int)rank * 128, wn = pt.col0 + (int)rank * hb;
+        int ka = 0;
+        for (int kb = 0; kb < KB; ++kb) {
+          pair_wait(&ctl->wempty[rs], rph ^ 1);
+          mbar_arrive_expect_tx(&ctl->wfull[rs], (uint32_t)wstage);
+          for (int h = 0; h < NH; ++h)
+            tma_load_2d(sW + rs * wstage + h * hb * kRecBytes, wmap, kb * kRecBytes, wn + h * BN, &ctl->wfull[rs]);
+          if (++rs == (uint32_t)RW) { rs = 0; rph ^= 1; }
+          for (int j = 0; j < 4; ++j, ka += kBK) {
+            pair_wait(&ctl->oempty[s], ph ^ 1);
+            if (rank == 0) {
+              mbar_arrive_expect_tx(&ctl->ofull[s], (uint32_t)kATileBytes);
+              tma_load_2d(sO + s * ostage, &map_a, ka, am, &ctl->ofull[s]);
+            } else {
+              mbar_arrive_expect_tx_remote(leader_ofull + 8u * s, (uint32_t)kATileBytes);
+              tma_load_2d_pair(sO + s * ostage, &map_a, ka, am, leader_ofull + 8u * s);
+            }
+            if (++s == (uint32_t)S) { s = 0; ph ^= 1; }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---------------- MMA issuer ----------------
+      const uint32_t idesc = idesc_f16_f32_m256(BN);
+      const uint64_t a0 = smem_desc_sw128(sO), b0 = smem_desc_sw128(sO + kATileBytes);
+      const uint64_t step = (uint64_t)(ostage >> 4), bhalf = (uint64_t)((hb * 128) >> 4);
+      uint32_t s = 0, ph = 0, it = 0;
+      uint64_t off = 0;
+      for (int t = pair; t < T; t += npairs) {
+        PairTile pt;
+        if (!pair_tile(pw, t, M, TM, TN, width, pt)) continue;
+        const uint32_t b = nacc == 2 ? (it & 1) : 0u, u = nacc == 2 ? (it >> 1) : it;
+        pair_wait(&ctl->acc_empty[b], (u & 1) ^ 1);
+        tc_fence_after();
+        const uint32_t d = tmem + b * (uint32_t)width;
+        for (int kt = 0; kt < nkt; ++kt) {
+          pair_wait(&ctl->ofull[s], ph);
+          tc_fence_after();
+          for (int h = 0; h < NH; ++h) {
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              tc2_mma_f16(d + (uint32_t)(h * BN), a0 + off + 2 * kk, b0 + off + h * bhalf + 2 * kk, idesc,
+                          (kt | kk) != 0 ? 1u : 0u);
+          }
+          tc2_commit_pair(&ctl->oempty[s]);      // both CTAs may refill the stage once these MMAs are done
+          off += step;
+          if (++s == (uint32_t)S) { s = 0; ph ^= 1; off = 0; }
+        }
+        tc2_commit_pair(&ctl->acc_full[b]);
+        ++it;
+      }
+    }
+  } else if (warp < 2 + DW) {
+    // ---------------- decode ----------------
+    // DW / 8 groups of 8 warps take turns by K step (group g decodes the steps
+    // q with q % groups == g), so several stages are decoded at once.  In a
+    // group, one thread decodes one (row, sub-block) item; 128 rows per pass,
+    // a CTA with 2 x 128 rows takes two passes.
+    constexpr int kGroups = DW / 8;
+    const int grp = (warp - 2) >> 3;
+    const int dt = ((warp - 2) & 7) * 32 + lane;
+    const int h = dt & 1, n = dt >> 1;
+    const uint32_t leader_ofull = mapa_shared(smem_u32(&ctl->ofull[0]), 0);
+    uint32_t s = (uint32_t)grp, ph = 0, rs = 0, rph = 0;   // this group's first step is q = grp (< S)
+    for (int t = pair; t < T; t += npairs) {
+      PairTile pt;
+      if (!pair_tile(pw, t, M, TM, TN, width, pt)) continue;
+      for (int kb = 0; kb < KB; ++kb) {
+        pair_wait(&ctl->wfull[rs], rph);
+        uint4 hd[2];
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          const int rl = p * 128 + n;
+          if (rl < rows) hd[p] = *reinterpret_cast<const uint4*>(sW + rs * wstage + rl * kRecBytes);
+        }
+        for (int j = grp; j < 4; j += kGroups) {
+          pair_wait(&ctl->oempty[s], ph ^ 1);
+#pragma unroll
+          for (int p = 0; p < 2; ++p) {
+            const int rl = p * 128 + n;
+            if (rl < rows) {
+              const int half = rl >= hb ? 1 : 0, rr = rl - half * hb;
+              const uint8_t* rec = sW + rs * wstage + rl * kRecBytes;
+              const uint4 q0 = *reinterpret_cast<const uint4*>(rec + 16 + 32 * j);
+              const uint4 q1 = *reinterpret_cast<const uint4*>(rec + 32 + 32 * j);
+              const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+              decode_part<4>(hd[p], qw, h, j, 0, sO + s * ostage + kATileBytes + half * hb * 128 + rr * 128, rr);
+            }
+          }
+          fence_proxy_async_smem();               // generic-proxy writes -> visible to the tensor core
+          __syncwarp();
+          if (lane == 0) {
+            if (rank == 0)
+              mbar_arrive(&ctl->ofull[s]);
+            else
+              mbar_arrive_remote(leader_ofull + 8u * s);
+          }
+          s += kGroups;                           // next step of this group
+          if (s >= (uint32_t)S) { s -= (uint32_t)S; ph ^= 1; }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->wempty[rs]);
+        if (++rs == (uint32_t)RW) { rs = 0; rph ^= 1; }
+      }
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    grid_dep_wait();                              // row scales come from the preceding kernel
+    const int ew = warp - 2 - DW;                 // 0..3
+    const int sp = warp & 3;                      // TMEM sub-partition this warp may read
+    float* tile = sEpi + ew * kEpiTileFloats;
+    const uint32_t leader_acc_empty = mapa_shared(smem_u32(&ctl->acc_empty[0]), 0);
+    uint32_t it = 0;
+    for (int t = pair; t < T; t += npairs) {
+      PairTile pt;
+      if (!pair_tile(pw, t, M, TM, TN, width, pt)) continue;
+      const uint32_t b = nacc == 2 ? (it & 1) : 0u, u = nacc == 2 ? (it >> 1) : it;
+      pair_wait(&ctl->acc_full[b], u & 1);
+      tc_fence_after();
+      const int mrow0 = pt.am0 + (int)rank * 128 + sp * 32;
+      const float rsc = (mrow0 + lane) < pt.mhi ? rowscale[mrow0 + lane] : 0.f;
+      for (int ch = 0; ch < width / 32; ++ch) {
+        uint32_t v[32];
+        tmem_ld32(tmem + ((uint32_t)(sp * 32) << 16) + b * (uint32_t)width + (uint32_t)(ch * 32), v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) tile[lane * 33 + c] = __uint_as_float(v[c]) * rsc;
+        __syncwarp();
+        const int nn = pt.col0 + ch * 32 + lane;
+        const float bv = (bias && nn < N) ? bias[nn] : 0.f;
+        for (int r = 0; r < 32; ++r) {
+          const int m = mrow0 + r;
+          if (m < pt.mhi && nn < N) y[(int64_t)m * N + nn] = tile[r * 33 + lane] + bv;
+        }
+        __syncwarp();
+      }
+      tc_fence_before();                          // this warp's TMEM reads are complete
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0)
+          mbar_arrive(&ctl->acc_empty[b]);
+        else
+          mbar_arrive_remote(leader_acc_empty + 8u * b);
+      }
+      ++it;
+    }
+  }
+  tc_fence_before();
+  cluster_sync_all();                             // no arrival or MMA read of the peer's memory is outstanding
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -469,6 +868,182 @@ int launch_gemm(const CUtensorMap& map_a, const uint8_t* w, int64_t m, int64_t n
   if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemm launch: %s", cudaGetErrorString(e));
   return xm_check_launch("qgemm");
 }
+
+// ---- CTA-pair kernel ----
+#ifndef XM_PAIR_DW
+#define XM_PAIR_DW 16   // decode warps per CTA: groups of 8 that take turns by K step
+#endif
+constexpr int kPairDW = XM_PAIR_DW;
+static_assert(kPairDW == 8 || kPairDW == 16, "decode warps");
+constexpr int kPairRaw = 2;                     // raw record stages (double buffer)
+
+struct PairCfg {
+  int BN, NH, S, RW, smem;
+};
+
+int pair_smem_bytes(int BN, int NH, int S, int RW) {
+  const int rows = NH * (BN / 2);
+  return 1024 + S * (kATileBytes + rows * 128) + RW * rows * kRecBytes + kPairEpiWarps * kEpiTileFloats * 4 +
+         (int)sizeof(PairSmem);
+}
+
+// Deepest operand ring that fits; S = 0 if fewer than 3 stages fit.
+PairCfg pair_stages(int BN, int NH) {
+  int S = kMaxStages;
+  while (S > 2 && pair_smem_bytes(BN, NH, S, kPairRaw) > 227 * 1024) --S;
+  if (S < 3) S = 0;
+  return {BN, NH, S, kPairRaw, pair_smem_bytes(BN, NH, S, kPairRaw)};
+}
+
+template <int NMAP>
+const void* pair_kernel() {
+  return reinterpret_cast<const void*>(k_qgemm_q4k_pair<kPairDW, NMAP>);
+}
+
+// How many CTA pairs of a configuration can be resident at once (0 if the
+// device cannot launch the pair kernel); cached per device and configuration.
+int pair_capacity(const PairCfg& cfg) {
+  static int cache[16][2][9];
+  static bool known[16][2][9];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int a = cfg.NH - 1, b = cfg.BN / 32;
+  if (dev >= 0 && dev < 16 && known[dev][a][b]) return cache[dev][a][b];
+  int n = 0;
+  const void* fn = pair_kernel<1>();
+  if (cfg.S >= 3 && cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, cfg.smem) == cudaSuccess) {
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3(2);
+    lc.blockDim = dim3(pair_threads(kPairDW));
+    lc.dynamicSmemBytes = cfg.smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, fn, &lc) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();
+  if (dev >= 0 && dev < 16) {
+    cache[dev][a][b] = n;
+    known[dev][a][b] = true;
+  }
+  return n;
+}
+
+// Tile shape for `mtiles` 256-row tiles of output width n: BN (multiple of 32,
+// <= 256) and NH (1: double-buffered accumulators; 2: one accumulator of 2BN
+// columns).  Estimated time per pair: rounds x main loop (MMA per K step plus
+// a fixed cost) plus the epilogues that do not overlap.
+PairCfg choose_pair(int64_t mtiles, int64_t n, int64_t k, int pairs) {
+  PairCfg best{0, 0, 0, 0, 0};
+  double best_t = 1e30;
+  const double nkt = (double)(k / kBK);
+  for (int nh = 1; nh <= 2; ++nh)
+    for (int bn = 256; bn >= 32; bn -= 32) {
+      if (nh == 2 && bn < 128) continue;
+      const PairCfg c = pair_stages(bn, nh);
+      if (c.S < 3) continue;
+      const int width = nh * bn;
+      const int64_t tiles = mtiles * ((n + width - 1) / width);
+      const double rounds = (double)((tiles + pairs - 1) / pairs);
+      const double main_us = nkt * (0.26 * width / 256.0 + 0.06);
+      const double epi_us = width * 0.0128;
+      const double t = rounds * main_us + (nh == 2 ? rounds : 1.0) * epi_us;
+      if (t < best_t) {
+        best_t = t;
+        best = c;
+      }
+    }
+  return best;
+}
+
+int encode_w_records(CUtensorMap* map, const uint8_t* w, int64_t n, int64_t k, int rows_per_box) {
+  EncodeTiledFn encode = get_encode();
+  if (!encode) return xm_set_error(XM_ERR_CUDA, "qgemm: cuTensorMapEncodeTiled unavailable");
+  const int64_t row_bytes = (k / 256) * kRecBytes;
+  const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)n};
+  const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  const cuuint32_t box[2] = {(cuuint32_t)kRecBytes, (cuuint32_t)rows_per_box};
+  const cuuint32_t es[2] = {1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w), dims, strides, box, es,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return xm_set_error(XM_ERR_CUDA, "qgemm: weight tensor map (%d)", (int)r);
+  return XM_OK;
+}
+
+template <int NMAP>
+int launch_pair(const CUtensorMap& map_a, const PairW<NMAP>& pw, int64_t m, int64_t n, int64_t k, int tm,
+                const PairCfg& cfg, int pairs, const float* rowscale, const float* bias, float* y, cudaStream_t st) {
+  const void* fn = pair_kernel<NMAP>();
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, cfg.smem);
+  if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemm: smem attribute: %s", cudaGetErrorString(e));
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3((unsigned)(2 * pairs));
+  lc.blockDim = dim3(pair_threads(kPairDW));
+  lc.dynamicSmemBytes = cfg.smem;
+  lc.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 2;
+  e = cudaLaunchKernelEx(&lc, k_qgemm_q4k_pair<kPairDW, NMAP>, map_a, pw, (int)m, (int)n, (int)k, cfg.BN, cfg.NH,
+                         cfg.S, cfg.RW, tm, rowscale, bias, y);
+  if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemm pair launch: %s", cudaGetErrorString(e));
+  return xm_check_launch("qgemm pair");
+}
+
+// Dense GEMM on the CTA-pair kernel.  Returns 1 (nothing launched) when the
+// device cannot hold a pair, so the caller can use the single-CTA kernel.
+int launch_pair_gemm(const CUtensorMap& map_a, const uint8_t* w, int64_t m, int64_t n, int64_t k,
+                     const float* rowscale, const float* bias, float* y, cudaStream_t st) {
+  const int cap = pair_capacity(pair_stages(256, 1));
+  if (cap < 1) return 1;
+  const int64_t mtiles = (m + 255) / 256;
+  const PairCfg cfg = choose_pair(mtiles, n, k, cap);
+  if (cfg.S < 3) return 1;
+  const int cap_cfg = pair_capacity(cfg);
+  if (cap_cfg < 1) return 1;
+  PairW<1> pw{};
+  int rc = encode_w_records(&pw.map[0], w, n, k, cfg.BN / 2);
+  if (rc) return rc;
+  pw.groups = 1;
+  const int64_t tiles = mtiles * ((n + cfg.NH * cfg.BN - 1) / (cfg.NH * cfg.BN));
+  const int pairs = (int)std::min<int64_t>(tiles, cap_cfg);
+  return launch_pair<1>(map_a, pw, m, n, k, (int)mtiles, cfg, pairs, rowscale, bias, y, st);
+}
+
+// Grouped GEMM (MoE experts) on the CTA-pair kernel; 1 if not possible.
+int launch_pair_grouped(const CUtensorMap& map_a, const uint8_t* const* h_w, const int* d_cnt, const int* d_off, int G,
+                        int64_t P, int64_t n, int64_t k, int64_t max_rows, int64_t expect_rows,
+                        const float* rowscale, float* y, cudaStream_t st) {
+  const int cap = pair_capacity(pair_stages(256, 1));
+  if (cap < 1) return 1;
+  const PairCfg cfg = choose_pair((int64_t)G * ((expect_rows + 255) / 256), n, k, cap);
+  if (cfg.S < 3) return 1;
+  const int cap_cfg = pair_capacity(cfg);
+  if (cap_cfg < 1) return 1;
+  PairW<kMaxGroups> pw{};
+  for (int g = 0; g < G; ++g) {
+    int rc = encode_w_records(&pw.map[g], h_w[g], n, k, cfg.BN / 2);
+    if (rc) return rc;
+  }
+  pw.cnt = d_cnt;
+  pw.off = d_off;
+  pw.groups = G;
+  const int tm = (int)((max_rows + 255) / 256);
+  const int64_t tiles = (int64_t)G * tm * ((n + cfg.NH * cfg.BN - 1) / (cfg.NH * cfg.BN));
+  const int pairs = (int)std::min<int64_t>(tiles, cap_cfg);
+  return launch_pair<kMaxGroups>(map_a, pw, P, n, k, tm, cfg, pairs, rowscale, nullptr, y, st);
+}
 }  // namespace
 
 int qgemm_q4k_grouped(const __half* a16, const float* rowscale, int64_t P, int64_t K, int64_t N,
@@ -484,6 +1059,8 @@ int qgemm_q4k_grouped(const __half* a16, const float* rowscale, int64_t P, int64
   CUtensorMap map_a;
   int rc = encode_a16(&map_a, a16, P, K);
   if (rc) return rc;
+  rc = launch_pair_grouped(map_a, h_w, d_cnt, d_off, G, P, N, K, max_rows, expect_rows, rowscale, y, st);
+  if (rc != 1) return rc;
   // tile shape for the expected rows per group, grid for the worst case
   TileCfg cfg = choose_tile(expect_rows, N * G, K, sm_count_dev());
   const dim3 grid((unsigned)((N + cfg.BN - 1) / cfg.BN), (unsigned)((max_rows + cfg.MT * 128 - 1) / (cfg.MT * 128)),
@@ -529,10 +1106,12 @@ extern "C" int xm_qgemm(int qtype, const void* d_w, int64_t w_bytes, int64_t n, 
   int rc = xm_check_launch("qgemm prep");
   if (rc) return rc;
 
-  const TileCfg cfg = choose_tile(m, n, k, sm_count_dev());
   CUtensorMap map_a;
   rc = encode_a16(&map_a, x16, m, k);
   if (rc) return rc;
+  rc = launch_pair_gemm(map_a, (const uint8_t*)d_w, m, n, k, rowscale, d_bias, d_y, st);
+  if (rc != 1) return rc;
+  const TileCfg cfg = choose_tile(m, n, k, sm_count_dev());
   const dim3 grid((unsigned)((n + cfg.BN - 1) / cfg.BN), (unsigned)((m + cfg.MT * 128 - 1) / (cfg.MT * 128)));
   return launch_gemm(map_a, (const uint8_t*)d_w, m, n, k, cfg, grid, rowscale, d_bias, d_y,
                      GemmGroups{}, st);
