@@ -158,6 +158,30 @@ def time_cpu_port(w32, x, budget_s=10.0, max_iters=5000, min_iters=20):
     return dt, it
 
 
+def time_cpu_dequant(raw, rows=1024):
+    """The reference's load-time step, gguf_dequant.dequantize (single-threaded
+    numpy, restated in oracle/), timed on the first `rows` rows of the weight
+    and scaled per byte to the whole weight: returns seconds for all N rows."""
+    from oracle import gguf_dequant_oracle as O
+    rb = (K // 256) * 144
+    rows = min(rows, N)
+    part = bytes(raw[: rows * rb])
+    t0 = time.perf_counter()
+    O.dequantize(part, QTYPE, (rows, K))
+    return (time.perf_counter() - t0) * (N / rows)
+
+
+def cpu_dequant_fields(raw, dt_matmul):
+    """The three CPU figures: dequantize alone, the fp32 matmul alone (the
+    `value`), and the two back to back (a path that dequantizes per call)."""
+    t_deq = time_cpu_dequant(raw)
+    return {"dequant": {"GBps": round(W_BYTES / t_deq / 1e9, 5), "s_per_weight": round(t_deq, 3), "threads": 1,
+                        "sample": f"1024 of {N} rows, scaled per byte"},
+            "dequant_plus_matmul": {"GBps": round(W_BYTES / (t_deq + dt_matmul) / 1e9, 5),
+                                    "note": "per call if the weight were dequantized every step; the reference "
+                                            "dequantizes once at load, so its per-step cost is the matmul"}}
+
+
 # ---------------------------------------------------------------------------
 def dist_setup(backend):
     import torch
@@ -196,7 +220,8 @@ def run_reference(args):
            "config": config({"reference_path": "numpy port of LinearOp.forward (ops.py:62-67) on the weight "
                                                "dequantized at load (gguf_dequant.py:309-341), host CPU"}),
            "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": cores, "kind": "port",
-                            "sample": f"{args.steps} steps of fp32 (1x{K}) @ ({K}x{N}) numpy/BLAS"},
+                            "sample": f"{args.steps} steps of fp32 (1x{K}) @ ({K}x{N}) numpy/BLAS",
+                            **cpu_dequant_fields(raw, dt)},
            "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
 
@@ -349,7 +374,8 @@ def run_ours(args):
         w32, xc = cpu_port_setup(raw, xb)
         dt, it = time_cpu_port(w32, xc)
         cpu = {"value": round(W_BYTES / dt / 1e9, 3), "unit": UNIT, "cores": blas_threads(), "kind": "port",
-               "sample": f"{it} steps of fp32 (1x{K}) @ ({K}x{N}) numpy/BLAS on the dequantized weight (~10 s)"}
+               "sample": f"{it} steps of fp32 (1x{K}) @ ({K}x{N}) numpy/BLAS on the dequantized weight (~10 s)",
+               **cpu_dequant_fields(raw, dt)}
 
     decode = None if args.no_decode else decode_section(args, rank, world, dev, peaks)
     moe = None if args.no_moe else (moe_section(dev) if world == 1 else moe_ep_section(dev, rank, world))
