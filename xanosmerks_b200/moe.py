@@ -141,7 +141,6 @@ class MoELayerEP:
 
     def forward_device(self, x: torch.Tensor) -> torch.Tensor:
         """x: this rank's tokens, CUDA (..., H) -> fp32 CUDA tensor of the same shape."""
-        import torch.distributed as dist
         H, F, E, k = self.hidden, self.intermediate, self.num_experts, self.num_experts_per_tok
         W, El = self.world, self.e_local
         if x.shape[-1] != H:
@@ -158,30 +157,52 @@ class MoELayerEP:
         with torch.cuda.device(dev):
             check(lib.xm_moe_dispatch(xf.data_ptr(), _DT[xf.dtype], T, H, self.gate.data_ptr(), E, k, F,
                                       send.data_ptr(), cnt.data_ptr(), ws.data_ptr(), ws.numel(), st), "moe_dispatch")
-            recv_cnt = torch.empty(E, dtype=torch.int32, device=dev)   # [source rank][local expert]
-            dist.all_to_all_single(recv_cnt, cnt, group=self.pg)
-            c_send = cnt.view(W, El).sum(1).cpu().tolist()
-            rc = recv_cnt.cpu()
-            c_recv = rc.view(W, El).sum(1).tolist()
-            R = int(sum(c_recv))
-            recv = torch.empty((R, H), dtype=xf.dtype, device=dev)
-            dist.all_to_all_single(recv, send, c_recv, c_send, group=self.pg)
-            off = torch.cumsum(rc, 0) - rc
-            g_cnt = rc.to(dev)
-            g_off = off.to(torch.int32).to(dev)
-            rows = torch.empty((R, H), dtype=torch.float32, device=dev)
-            if R:
-                ews = torch.empty(lib.xm_moe_experts_workspace_size(R, H, F), dtype=torch.uint8, device=dev)
-                check(lib.xm_moe_experts(recv.data_ptr(), _DT[xf.dtype], R, H, F, W * El, g_cnt.data_ptr(),
-                                         g_off.data_ptr(), self._p1, self._p3, self._p2, self.qtype,
-                                         int(rc.max()), rows.data_ptr(), ews.data_ptr(), ews.numel(), st),
-                      "moe_experts")
-            back = torch.empty((T * k, H), dtype=torch.float32, device=dev)
-            dist.all_to_all_single(back, rows, c_send, c_recv, group=self.pg)
+            keep = []                                  # device temporaries the experts kernel reads
+
+            def run_experts(recv, rc, off):
+                R = recv.shape[0]
+                rows = torch.empty((R, H), dtype=torch.float32, device=dev)
+                if R:
+                    g_cnt = rc.to(dev)
+                    g_off = off.to(torch.int32).to(dev)
+                    ews = torch.empty(lib.xm_moe_experts_workspace_size(R, H, F), dtype=torch.uint8, device=dev)
+                    keep.extend((g_cnt, g_off, ews))
+                    check(lib.xm_moe_experts(recv.data_ptr(), _DT[xf.dtype], R, H, F, W * El, g_cnt.data_ptr(),
+                                             g_off.data_ptr(), self._p1, self._p3, self._p2, self.qtype,
+                                             int(rc.max()), rows.data_ptr(), ews.data_ptr(), ews.numel(), st),
+                          "moe_experts")
+                return rows
+
+            back = ep_exchange(send, cnt, W, El, self.pg, run_experts)
             out = torch.empty((T, H), dtype=torch.float32, device=dev)
             check(lib.xm_moe_combine(back.data_ptr(), T, H, E, k, F, ws.data_ptr(), out.data_ptr(), st),
                   "moe_combine")
         return out.reshape(x.shape)
 
 
-__all__ = ["MoELayer", "MoELayerEP"]
+def ep_exchange(send, cnt, world: int, e_local: int, group, run_experts):
+    """The host side of expert parallelism between the dispatch and the combine.
+
+    ``send``: this rank's routed rows in ascending expert order (expert e on
+    rank e // e_local), ``cnt``: int32 rows per expert.  Exchanges the counts
+    and the rows (``all_to_all_single``), calls ``run_experts(recv, rc, off)``
+    on the received rows, which arrive grouped by (source rank, local expert)
+    with counts ``rc`` and offsets ``off`` (host int tensors), and sends the
+    fp32 result rows back; returns them in ``send``'s order.  The tensors may
+    live on the GPU (NCCL) or the CPU (gloo)."""
+    import torch.distributed as dist
+    recv_cnt = torch.empty_like(cnt)                       # [source rank][local expert]
+    dist.all_to_all_single(recv_cnt, cnt, group=group)
+    c_send = cnt.view(world, e_local).sum(1).cpu().tolist()
+    rc = recv_cnt.cpu()
+    c_recv = rc.view(world, e_local).sum(1).tolist()
+    recv = send.new_empty((int(sum(c_recv)), send.shape[1]))
+    dist.all_to_all_single(recv, send, c_recv, c_send, group=group)
+    off = torch.cumsum(rc, 0) - rc
+    rows = run_experts(recv, rc, off)
+    back = rows.new_empty((send.shape[0], rows.shape[1]))
+    dist.all_to_all_single(back, rows, c_send, c_recv, group=group)
+    return back
+
+
+__all__ = ["MoELayer", "MoELayerEP", "ep_exchange"]
