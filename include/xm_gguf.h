@@ -40,6 +40,12 @@ extern "C" {
 #define XM_DT_F16 1
 #define XM_DT_BF16 2
 
+/* expert activations of the MoE entry points (primitives.py:37-62 apply_activation) */
+#define XM_ACT_SILU 0     /* x / (1 + exp(-x)); also the reference's "swish" */
+#define XM_ACT_GELU 1     /* 0.5 x (1 + tanh(0.7978845608 (x + 0.044715 x^3))) */
+#define XM_ACT_RELU 2     /* max(x, 0) */
+#define XM_ACT_IDENTITY 3 /* x */
+
 /* activation prologues of xm_qgemv_ex */
 #define XM_PRO_NONE 0    /* v = x */
 #define XM_PRO_RMSNORM 1 /* v = (x / sqrt(mean(x^2) + eps)) * norm_w */
@@ -55,6 +61,12 @@ const char* xm_last_error(void);
  * inside a kernel gave up (XM_DEVERR_TIMEOUT = 1) instead of hanging.  With
  * clear != 0 the word is reset.  Returns the word (>= 0) or XM_ERR_CUDA. */
 int xm_device_status(int clear);
+
+/* Stream-ordered read of the same word: enqueues a copy of the current
+ * device's error word into *h_word (pinned host memory) on `stream`, after the
+ * work queued before it; read *h_word once the stream has been synchronised
+ * (and clear a non-zero word with xm_device_status(1)). */
+int xm_device_status_async(int* h_word, void* stream);
 
 /* Block geometry of a type: elements per block and bytes per block record.
  * Replaces the lookup in GGUF_TYPE_BLOCK_SIZE (dtype_map.py:68-79). */
@@ -83,9 +95,11 @@ int xm_dequantize(int qtype, const void* d_raw, int64_t raw_bytes, int64_t n_ele
  * never written back.
  *
  * `d_workspace` (16-byte aligned, >= xm_qgemv_workspace_size(k, m) bytes)
- * holds the activation split of the integer-dot path; with NULL the call takes
- * the exact path (each weight rounded to the reference's fp16 value).  Results
- * of both paths are within 1e-3 of the reference (max abs error / max |y|).
+ * holds the activation split of the integer-dot path.  With NULL, shapes whose
+ * split needs the workspace take the exact path (each weight rounded to the
+ * reference's fp16 value); Q4_K with m = 1 and k = 4096 splits inside its one
+ * kernel and takes the integer-dot path either way.  Results of both paths
+ * are within 1e-3 of the reference (max abs error / max |y|).
  *
  * Replaces the decode-time `x @ W.T` on dequantized weights: ops.py:62-67
  * `LinearOp.forward`, forward.py:93-101 (MLP), attention.py:47-51/:135
@@ -129,8 +143,9 @@ int xm_qgemv_ex(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t 
                 const float* d_norm_w, float eps, const float* d_bias, float* d_y, int accumulate,
                 void* d_workspace, int64_t workspace_bytes, void* stream);
 
-/* The exact path of xm_qgemv alone (every weight rounded to the reference's
- * fp16 value, fp32 products); the cross-check of the integer-dot path. */
+/* The exact path alone, for every type and shape (every weight rounded to
+ * the reference's fp16 value, fp32 products): the cross-check of the
+ * integer-dot path.  Same arguments and limits as xm_qgemv, no workspace. */
 int xm_qgemv_exact(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k,
                    const void* d_x, int x_dtype, int64_t m, const float* d_bias, float* d_y,
                    void* stream);
@@ -138,13 +153,17 @@ int xm_qgemv_exact(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64
 /*
  * Prefill GEMM on 5th-generation tensor cores: y[m][n] = sum_k x[m][k] *
  * W[n][k] (+ bias[n]) for any m >= 1 (meant for m >= 64), x row-major [m][k]
- * of x_dtype (16-byte aligned), y row-major [m][n] fp32.  Each weight is
- * decoded to the reference's fp16 value, x is converted to fp16 with an exact
- * power-of-two scale per row, tcgen05.mma accumulates in fp32: the result
- * differs from the reference's fp32 `x @ W.T` only in summation order.
+ * of x_dtype (16-byte aligned), y row-major [m][n] fp32, W GGUF blocks of any
+ * block-quantized type (Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q8_1, Q2_K ... Q8_K)
+ * with k a multiple of 256.  Each weight is decoded to the reference's fp16
+ * value, x is converted to fp16 with an exact power-of-two scale per row,
+ * tcgen05.mma accumulates in fp32: the result differs from the reference's
+ * fp32 `x @ W.T` only in summation order.  A weight row must be a whole
+ * number of 16-byte units (true for every type when k % 2048 == 0; Q6_K and
+ * Q3_K rows of k = 1792, for example, are not): other shapes return
+ * XM_ERR_UNSUPPORTED and callers use xm_qgemv on groups of 8 rows.
  * `d_workspace` (256-byte aligned, >= xm_qgemm_workspace_size(m, k) bytes)
- * holds the converted activations.  Types other than Q4_K return
- * XM_ERR_UNSUPPORTED (callers fall back to xm_qgemv on row groups).
+ * holds the converted activations.
  *
  * Replaces the prefill `x @ W.T` of LinearOp.forward (ops.py:62-67) and of
  * the MLP / attention projections (forward.py:93-101, attention.py:47-51).
@@ -155,14 +174,43 @@ int xm_qgemm(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k,
              void* d_workspace, int64_t workspace_bytes, void* stream);
 
 /*
- * Sparse mixture-of-experts block (Mixtral-style SwiGLU experts):
+ * xm_qgemm with the prologues and the residual add of xm_qgemv_ex:
+ *   y[m][n] (+)= sum_k pro(x)[m][k] * W[n][k] (+ bias[n])
+ * `prologue` is XM_PRO_NONE, XM_PRO_RMSNORM (weight d_norm_w [k], eps) or
+ * XM_PRO_SWIGLU (rows of x hold gate then up, 2k values); `x_stride` is the
+ * row pitch of x in elements.  The prologue runs in fp32 before the fp16
+ * conversion of the activation.
+ *
+ * Replaces FusedRMSNormLinearOp.forward (ops.py:107-123) for many rows, and
+ * the prefill MLP `swiglu(gate, up) @ W_down.T` with its residual add
+ * (forward.py:97-101, :116).
+ */
+int xm_qgemm_ex(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k,
+                const void* d_x, int x_dtype, int64_t m, int64_t x_stride, int prologue,
+                const float* d_norm_w, float eps, const float* d_bias, float* d_y, int accumulate,
+                void* d_workspace, int64_t workspace_bytes, void* stream);
+
+/*
+ * RMSNorm of m rows of x (row pitch x_stride elements): out[m][k] fp32 =
+ * (x / sqrt(mean(x^2) + eps)) * norm_w, in the reference's order
+ * (primitives.py:20-23, ops.py:115-117).  The norm of FusedRMSNormLinearOp
+ * for weights whose matmul has no fused prologue (dense weights, block types
+ * without an integer-dot GEMV or tensor-core GEMM at that shape).
+ */
+int xm_rmsnorm(const void* d_x, int x_dtype, int64_t m, int64_t k, int64_t x_stride,
+               const float* d_norm_w, float eps, float* d_out, void* stream);
+
+/*
+ * Sparse mixture-of-experts block (Mixtral-style gated experts):
  *   out[t] = sum over the k experts e chosen for token t (ascending e) of
- *            w[t][e] * ((silu(x_t @ W1_e.T) * (x_t @ W3_e.T)) @ W2_e.T)
+ *            w[t][e] * ((act(x_t @ W1_e.T) * (x_t @ W3_e.T)) @ W2_e.T)
+ * with act = XM_ACT_* (`activation`; silu for Mixtral)
  * with router logits x @ gate.T (gate fp32 [E][H]), the k largest logits per
  * token and a softmax over those k (over all E when k == E).  x row-major
  * [T][H] of x_dtype, out fp32 [T][H].  h_w1/h_w3 ([F][H]) and h_w2 ([H][F])
- * are HOST arrays of E device pointers to GGUF blocks of `qtype` (Q4_K; other
- * types return XM_ERR_UNSUPPORTED).  E <= 32; H and F multiples of 256.
+ * are HOST arrays of E device pointers to GGUF blocks of `qtype` (any type
+ * that xm_qgemm takes at k = H and at k = F; others return
+ * XM_ERR_UNSUPPORTED).  E <= 32; H and F multiples of 256.
  * `d_workspace` (256-byte aligned, xm_moe_workspace_size bytes) holds the
  * routing, the gathered activations and the expert intermediates.  The whole
  * block runs on `stream` without host synchronisation: routing, a stable
@@ -174,7 +222,7 @@ int xm_qgemm(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k,
 int64_t xm_moe_workspace_size(int64_t T, int64_t H, int64_t F, int E, int k);
 int xm_moe_forward(const void* d_x, int x_dtype, int64_t T, int64_t H, const float* d_gate,
                    int E, int k, int64_t F, const void* const* h_w1, const void* const* h_w3,
-                   const void* const* h_w2, int qtype, float* d_out, void* d_workspace,
+                   const void* const* h_w2, int qtype, int activation, float* d_out, void* d_workspace,
                    int64_t workspace_bytes, void* stream);
 
 /*
@@ -189,7 +237,8 @@ int xm_moe_forward(const void* d_x, int x_dtype, int64_t T, int64_t H, const flo
  * xm_moe_experts on the received rows: G groups of rows [off[g], off[g] +
  * cnt[g]) (device arrays; typically one group per (source rank, local
  * expert)) through the SwiGLU expert of group g (host pointer arrays h_w1,
- * h_w3, h_w2 of G entries; Q4_K), fp32 rows out; max_rows bounds cnt[g].
+ * h_w3, h_w2 of G entries; types as for xm_moe_forward), fp32 rows out;
+ * max_rows bounds cnt[g].
  * After exchanging the result rows back into the send order, xm_moe_combine
  * forms out[t] = sum over the token's k rows, ascending expert, of row *
  * weight (moe.py:110-113), reading the routing from the dispatch workspace
@@ -201,8 +250,8 @@ int xm_moe_dispatch(const void* d_x, int x_dtype, int64_t T, int64_t H, const fl
 int64_t xm_moe_experts_workspace_size(int64_t P, int64_t H, int64_t F);
 int xm_moe_experts(const void* d_rows, int x_dtype, int64_t P, int64_t H, int64_t F, int G, const int* d_cnt,
                    const int* d_off, const void* const* h_w1, const void* const* h_w3, const void* const* h_w2,
-                   int qtype, int64_t max_rows, float* d_out, void* d_workspace, int64_t workspace_bytes,
-                   void* stream);
+                   int qtype, int activation, int64_t max_rows, float* d_out, void* d_workspace,
+                   int64_t workspace_bytes, void* stream);
 int xm_moe_combine(const float* d_rows, int64_t T, int64_t H, int E, int k, int64_t F, const void* d_workspace,
                    float* d_out, void* stream);
 
@@ -213,8 +262,10 @@ int xm_moe_combine(const float* d_rows, int64_t T, int64_t H, int E, int k, int6
  * built into this library, 320 KiB per GPU (limit: m <= 8 with k <= 16384;
  * larger requests return XM_ERR_INVALID).  The first call on each device
  * looks up that array's address (cudaGetSymbolAddress), so make it before any
- * stream capture.  Calls share the array: calls that overlap on the GPU race.
- * Nothing is allocated.  This entry point has no counterpart in the reference.
+ * stream capture; the address is kept for the life of the process, so a
+ * device reset (cudaDeviceReset) between calls is not supported.  Calls share
+ * the array: calls that overlap on the GPU race.  Nothing is allocated.  This
+ * entry point has no counterpart in the reference.
  */
 int xm_qgemv_noalloc(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k,
                      const void* d_x, int x_dtype, int64_t m, const float* d_bias, float* d_y,
@@ -229,7 +280,7 @@ int xm_qgemv_noalloc(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int
  * (vocab rows of D) -- the reference indexes its dequantized embedding
  * (forward.py:151).
  *
- * xm_attention: causal GQA attention of Lq (<= 8) new tokens per sequence.
+ * xm_attention: causal GQA attention of Lq (<= 64) new tokens per sequence.
  * qkv row b*Lq + j = [q | k | v] (Hq, Hk, Hk heads, fp32, row pitch
  * qkv_stride) of token j of sequence b at position pos0[b] + j, as the QKV
  * projection produced it.  Fused: rotate-half rotary embedding of q and k
@@ -275,10 +326,19 @@ int xm_argmax(const float* d_logits, int64_t B, int64_t V, int* d_out, void* str
  * closes the peer mappings and frees the buffer; call it on every rank after
  * all ranks have finished their last xm_allreduce_add (host barrier + device
  * synchronisation).  These entry points have no counterpart in the reference.
+ *
+ * xm_comm_open_local: rank `peer_rank`'s buffer is the one of `peer_comm`,
+ * created in this same process (one process driving several GPUs with peer
+ * access enabled), instead of an IPC mapping.  xm_comm_set_wait_limit sets
+ * the bounded wait of later xm_allreduce_add calls (1 us .. 60 s; default
+ * 2 s).  A call whose wait gave up leaves the comm's epochs out of step with
+ * the other ranks: destroy the comms of every rank and create new ones.
  */
 int64_t xm_comm_buffer_size(int64_t max_elems);
 int xm_comm_create(int world, int rank, int64_t max_elems, int nctas, void** out_comm, void* out_handle);
 int xm_comm_open_peer(void* comm, int peer_rank, const void* handle);
+int xm_comm_open_local(void* comm, int peer_rank, void* peer_comm);
+int xm_comm_set_wait_limit(void* comm, int64_t limit_ns);
 int xm_comm_destroy(void* comm);
 int xm_allreduce_add(void* comm, float* d_h, const float* d_part, int64_t n_elems, void* stream);
 

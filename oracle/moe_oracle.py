@@ -23,6 +23,30 @@ def silu(x):
     return x / (1.0 + np.exp(-x))
 
 
+def gelu(x):
+    """primitives.py:47-49 (tanh form)."""
+    return 0.5 * x * (1.0 + np.tanh(0.7978845608 * (x + 0.044715 * x ** 3)))
+
+
+def relu(x):
+    """primitives.py:58-59."""
+    return np.maximum(x, 0.0)
+
+
+def identity(x):
+    """primitives.py:60-61."""
+    return x
+
+
+# apply_activation's names (primitives.py:52-62)
+ACTS = {"silu": silu, "swish": silu, "gelu": gelu, "relu": relu, "identity": identity}
+
+
+def expert_ffn(xs, w1, w3, w2, act=silu):
+    """One expert on its rows (moe.py:106-109): act(xs @ w1.T) * (xs @ w3.T) @ w2.T."""
+    return (act(xs @ w1.T) * (xs @ w3.T)) @ w2.T
+
+
 def linear(x, w, b=None):
     """ops.py:62-67: fp32(x) @ W.T (+ b)."""
     y = np.asarray(x, dtype=np.float32) @ np.asarray(w, dtype=np.float32).T
@@ -56,8 +80,7 @@ def moe_forward(x, gate_w, experts, k, act=silu):
     if k == n_exp:
         wts = softmax(logits, axis=-1)
         for e in range(n_exp):
-            hdn = act(xf @ experts[e]["w1"].T) * (xf @ experts[e]["w3"].T)
-            out += (hdn @ experts[e]["w2"].T) * wts[:, e:e + 1]
+            out += expert_ffn(xf, experts[e]["w1"], experts[e]["w3"], experts[e]["w2"], act) * wts[:, e:e + 1]
         return out.reshape(b, s, h)
     se, sw, st, counts = route(logits, k)
     start = 0
@@ -65,8 +88,21 @@ def moe_forward(x, gate_w, experts, k, act=silu):
         end = start + int(counts[e])
         if end > start:
             tok = st[start:end]
-            xs = xf[tok]
-            hdn = act(xs @ experts[e]["w1"].T) * (xs @ experts[e]["w3"].T)
-            out[tok] += (hdn @ experts[e]["w2"].T) * sw[start:end, None]
+            y = expert_ffn(xf[tok], experts[e]["w1"], experts[e]["w3"], experts[e]["w2"], act)
+            out[tok] += y * sw[start:end, None]
         start = end
     return out.reshape(b, s, h)
+
+
+def combine(n_tok, h, routing, expert_out):
+    """The scatter-add of moe.py:110-113 given each expert's output rows in dispatch order:
+    ``routing`` = route(...), ``expert_out[e]`` = that expert's rows (ascending expert order)."""
+    se, sw, st, counts = routing
+    out = np.zeros((n_tok, h), dtype=np.float32)
+    start = 0
+    for e in range(len(counts)):
+        end = start + int(counts[e])
+        if end > start:
+            out[st[start:end]] += expert_out[e] * sw[start:end, None]
+        start = end
+    return out

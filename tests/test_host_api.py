@@ -54,9 +54,11 @@ def test_gguf_tensor_rejects_plain_types_before_any_device_work():
         GGUFTensor(b"", "F16", (1, 1))
 
 
-def test_linear_op_needs_a_quantized_weight():
-    with pytest.raises(TypeError):
-        LinearOp(np.zeros((4, 4), np.float32))
+def test_linear_op_checks_a_dense_weight_before_any_device_work():
+    """A dense float weight is accepted as in the reference (LinearOp(np.eye(4)), defaults.py:109-117);
+    its shape is checked on the host first."""
+    with pytest.raises(ValueError):
+        LinearOp(np.zeros((2, 4, 4), np.float32))
 
 
 @pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-GPU behaviour")
@@ -67,6 +69,8 @@ def test_product_path_fails_loudly_without_a_gpu():
         dequantize(raw, "Q4_K", (1, 256))
     with pytest.raises(Exception):
         GGUFTensor(raw, "Q4_K", (1, 256))
+    with pytest.raises(Exception):
+        LinearOp(np.eye(4, dtype=np.float32))
 
 
 def test_reference_arm_prints_the_contract_line():

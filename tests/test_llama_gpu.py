@@ -1,9 +1,11 @@
 """GPU parity: the Llama decoder step (fused-norm QKV GEMV, RoPE + KV append,
 GQA attention, O GEMV with residual, fused-norm gate/up GEMV, SwiGLU down GEMV
 with residual, output head, argmax) against the numpy oracle of the reference's
-TransformerModel forward with a KV cache, on the same GGUF weights.  Prefill
-runs in chunks of up to 8 tokens per sequence; decode steps run eagerly and
-from a captured CUDA graph."""
+TransformerModel forward with a KV cache, on the same GGUF weights.  Prompts
+of more than 8 tokens prefill on the tensor-core GEMM over all rows with the
+attention in chunks of up to 64 tokens (the 100-token case takes two chunks);
+shorter ones take the decode path 8 tokens at a time.  Decode steps run
+eagerly and from a captured CUDA graph."""
 
 import numpy as np
 import pytest
@@ -33,7 +35,7 @@ def oracle_weights(full):
             "lm_head": _f32(full["output"])}
 
 
-@pytest.mark.parametrize("batch,layers,prompt", [(1, 2, 11), (3, 1, 9)])
+@pytest.mark.parametrize("batch,layers,prompt", [(1, 2, 11), (3, 1, 9), (2, 1, 5), (1, 1, 100), (2, 1, 70)])
 def test_decoder_matches_oracle(batch, layers, prompt):
     cfg = LlamaConfig(num_layers=layers, vocab_size=4096)
     full = synth_llama_weights(cfg, seed=7, device="cuda")

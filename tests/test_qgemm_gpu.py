@@ -1,4 +1,7 @@
-"""GPU parity: tensor-core dequant-GEMM against the reference's fp32 ``x @ W.T``."""
+"""GPU parity: tensor-core dequant-GEMM against the reference's fp32 ``x @ W.T``
+(ops.py:62-67) on the weights the reference dequantizes (gguf_dequant.py:25-455),
+for every block type, with the RMSNorm / SwiGLU prologues and the residual add
+of ``xm_qgemm_ex`` (ops.py:107-123, forward.py:97-101, :116)."""
 
 import numpy as np
 import pytest
@@ -7,7 +10,8 @@ import torch
 from oracle import gguf_dequant_oracle as O
 from tests.helpers import GEMM_TOL, rel_err
 from xanosmerks_b200 import _lib
-from xanosmerks_b200.ops import GGUFTensor, LinearOp, qlinear
+from xanosmerks_b200.ops import GGUFTensor, LinearOp, gemm_supported, qlinear
+from xanosmerks_b200.qtypes import QUANT_NAMES, normalize
 from xanosmerks_b200.synth import make_weight
 
 pytestmark = pytest.mark.gpu
@@ -63,5 +67,102 @@ def test_q4k_gemm_matches_gemv_rows():
 
 def test_qgemm_rejects_bad_arguments():
     L = _lib.lib
-    assert L.xm_qgemm(14, None, 0, 4, 256, None, 0, 64, None, None, None, 0, None) == _lib.XM_ERR_UNSUPPORTED
+    for plain in (0, 1, 30, 16, 99):          # F32, F16, BF16, IQ2_XXS, unknown
+        assert L.xm_qgemm(plain, None, 0, 4, 256, None, 0, 64, None, None, None, 0, None) == _lib.XM_ERR_UNSUPPORTED
     assert L.xm_qgemm(12, None, 0, 4, 300, None, 0, 64, None, None, None, 0, None) == _lib.XM_ERR_INVALID
+    assert L.xm_qgemm(14, None, 0, 4, 256, None, 0, 64, None, None, None, 0, None) == _lib.XM_ERR_INVALID  # short
+
+
+def _gemm(W, x, prologue=_lib.PRO_NONE, norm=None, y=None, accumulate=False, eps=1e-5, bias=None):
+    """xm_qgemm_ex on a CUDA activation (fp32 rows of k, or 2k for SwiGLU)."""
+    n, k = W.shape
+    m = x.shape[0]
+    if y is None:
+        y = torch.zeros(m, n, dtype=torch.float32, device="cuda")
+    ws = torch.empty(_lib.lib.xm_qgemm_workspace_size(m, k), dtype=torch.uint8, device="cuda")
+    dt = {torch.float32: _lib.DT_F32, torch.bfloat16: _lib.DT_BF16, torch.float16: _lib.DT_F16}[x.dtype]
+    _lib.check(_lib.lib.xm_qgemm_ex(W.qtype.type_id, W.data.data_ptr(), W.nbytes, n, k, x.data_ptr(), dt, m,
+                                    x.shape[1], prologue, norm.data_ptr() if norm is not None else None, eps,
+                                    bias.data_ptr() if bias is not None else None, y.data_ptr(),
+                                    1 if accumulate else 0, ws.data_ptr(), ws.numel(),
+                                    torch.cuda.current_stream().cuda_stream), "qgemm_ex")
+    torch.cuda.synchronize()
+    return y
+
+
+@pytest.mark.parametrize("name", QUANT_NAMES)
+@pytest.mark.parametrize("m,n,k", [(300, 320, 2048), (77, 96, 256)])
+def test_gemm_every_block_type(name, m, n, k):
+    """Each of the twelve block types on the tensor cores (the generic decode for all but Q4_K), with
+    the column start rounded down to 16 bytes for records whose 256-wide column is not 16-byte sized."""
+    qt = normalize(name)
+    if not gemm_supported(qt, k):
+        pytest.skip(f"{name} rows of {k} are not whole 16-byte units")
+    raw, w = wref(name, n, k, 61)
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(62)).to(torch.bfloat16)
+    y = _gemm(GGUFTensor(raw, name, (n, k)), x.cuda()).cpu().numpy()
+    ref = x.float().numpy() @ w.T
+    e = rel_err(y, ref)
+    assert e < 1e-5, (name, e)       # fp16-exact operands: only the summation order differs
+
+
+@pytest.mark.parametrize("name,m,n,k", [("Q6_K", 512, 4096, 14336), ("Q5_K", 512, 4096, 4096),
+                                        ("Q6_K", 300, 4096, 4096), ("Q5_K", 200, 14336, 4096),
+                                        ("Q8_0", 256, 4096, 4096)])
+def test_gemm_config_shapes(name, m, n, k):
+    """The decode / prefill shapes of the Llama config: Q6_K down projection (K = 14336) and the
+    Q5_K / Q8_0 matrices, against the oracle."""
+    raw, w = wref(name, n, k, 71)
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(72)).to(torch.bfloat16)
+    y = qlinear(GGUFTensor(raw, name, (n, k)), x.cuda()).cpu().numpy()
+    ref = x.float().numpy() @ w.T
+    # fp16-exact operands; the fp32 accumulation-order difference grows with K
+    assert rel_err(y, ref) < 1e-5 * max(1.0, k / 4096), rel_err(y, ref)
+
+
+@pytest.mark.parametrize("name", ["Q4_K", "Q6_K", "Q4_0"])
+def test_gemm_rmsnorm_prologue_bias(name):
+    """FusedRMSNormLinearOp for many rows (ops.py:107-123): the norm in the activation preparation."""
+    m, n, k = 200, 256, 2048
+    raw, w = wref(name, n, k, 81)
+    rng = np.random.default_rng(82)
+    x = rng.standard_normal((m, k)).astype(np.float32) * 3.0
+    nw = (1 + 0.1 * rng.standard_normal(k)).astype(np.float32)
+    b = rng.standard_normal(n).astype(np.float32)
+    y = _gemm(GGUFTensor(raw, name, (n, k)), torch.from_numpy(x).cuda(), _lib.PRO_RMSNORM,
+              torch.from_numpy(nw).cuda(), bias=torch.from_numpy(b).cuda()).cpu().numpy()
+    rms = np.sqrt(np.mean(x ** 2, axis=-1, keepdims=True) + 1e-5)
+    ref = ((x / rms) * nw) @ w.T + b
+    assert rel_err(y, ref) < GEMM_TOL, rel_err(y, ref)
+
+
+@pytest.mark.parametrize("name", ["Q6_K", "Q5_K"])
+def test_gemm_swiglu_prologue_accumulate(name):
+    """The prefill MLP down projection with its residual add: h += swiglu(gate, up) @ W_down.T
+    (forward.py:97-101, :116), rows of x holding gate then up."""
+    m, n, k = 160, 512, 2048
+    raw, w = wref(name, n, k, 91)
+    rng = np.random.default_rng(92)
+    gu = rng.standard_normal((m, 2 * k)).astype(np.float32)
+    h0 = rng.standard_normal((m, n)).astype(np.float32)
+    y = torch.from_numpy(h0.copy()).cuda()
+    _gemm(GGUFTensor(raw, name, (n, k)), torch.from_numpy(gu).cuda(), _lib.PRO_SWIGLU, y=y, accumulate=True)
+    g, u = gu[:, :k], gu[:, k:]
+    ref = h0 + ((g / (1.0 + np.exp(-g))) * u) @ w.T
+    assert rel_err(y.cpu().numpy(), ref) < GEMM_TOL
+
+
+def test_gemm_row_pitch_not_16_bytes_falls_back_to_gemv():
+    """Q6_K rows of 1792 (a tensor-parallel K-slice of 14336 over 8 ranks) are 1470 bytes: the
+    GEMM reports UNSUPPORTED and qlinear multiplies them on the GEMV in groups of 8 rows."""
+    m, n, k = 40, 300, 1792
+    raw, w = wref("Q6_K", n, k, 95)
+    W = GGUFTensor(raw, "Q6_K", (n, k))
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(96)).to(torch.bfloat16).cuda()
+    ws = torch.empty(_lib.lib.xm_qgemm_workspace_size(m, k), dtype=torch.uint8, device="cuda")
+    y = torch.empty(m, n, dtype=torch.float32, device="cuda")
+    st = _lib.lib.xm_qgemm(14, W.data.data_ptr(), W.nbytes, n, k, x.data_ptr(), _lib.DT_BF16, m, None, y.data_ptr(),
+                           ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
+    assert st == _lib.XM_ERR_UNSUPPORTED and b"multiple of 16" in _lib.lib.xm_last_error()
+    yq = qlinear(W, x).cpu().numpy()
+    assert rel_err(yq, x.float().cpu().numpy() @ w.T) < 1e-3

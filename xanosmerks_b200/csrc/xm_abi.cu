@@ -56,7 +56,7 @@ bool host_qtype_geometry(int qtype, int* qk, int* rec) {
 
 extern "C" {
 
-int xm_abi_version(void) { return 1; }
+int xm_abi_version(void) { return 2; }
 
 const char* xm_last_error(void) { return g_last_error; }
 
@@ -70,6 +70,14 @@ int xm_device_status(int clear) {
     if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "device_status: %s", cudaGetErrorString(e));
   }
   return v;
+}
+
+int xm_device_status_async(int* h_word, void* stream) {
+  if (!h_word) return xm_set_error(XM_ERR_INVALID, "device_status_async: null destination");
+  cudaError_t e = cudaMemcpyFromSymbolAsync(h_word, g_xm_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost,
+                                            (cudaStream_t)stream);
+  if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "device_status_async: %s", cudaGetErrorString(e));
+  return XM_OK;
 }
 
 int xm_qtype_info(int qtype, int* qk, int* record_bytes) {

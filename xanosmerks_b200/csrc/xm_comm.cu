@@ -36,7 +36,7 @@ struct PeerTable {
   uint32_t* flags[kMaxRanks];    // each rank's flags[0][0]
 };
 
-constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr uint64_t kDefaultWaitLimitNs = 2000000000ull;
 
 XM_DEV uint64_t globaltimer_ns() {
   uint64_t t;
@@ -58,7 +58,8 @@ __global__ void __launch_bounds__(kCommThreads) k_allreduce_add(float* __restric
                                                                 int64_t max_elems, int world, int rank,
                                                                 PeerTable peers, uint32_t* __restrict__ my_flags,
                                                                 uint32_t* __restrict__ my_epochs,
-                                                                const float* __restrict__ my_recv) {
+                                                                const float* __restrict__ my_recv,
+                                                                uint64_t wait_limit_ns) {
   __shared__ uint32_t s_epoch;
   grid_dep_wait();
   const int j = blockIdx.x, tid = threadIdx.x;
@@ -81,11 +82,12 @@ __global__ void __launch_bounds__(kCommThreads) k_allreduce_add(float* __restric
     st_release_sys(peers.flags[tid] + j * kMaxRanks + rank, e);
   }
   if (tid < world) {
-    // bounded wait: a rank that never arrives costs 2 s and an error bit, not a hung GPU
+    // bounded wait: a rank that never arrives costs the wait limit (2 s unless
+    // set) and an error bit, not a hung GPU
     const uint32_t* f = my_flags + j * kMaxRanks + tid;
     const uint64_t t0 = globaltimer_ns();
     while ((int32_t)(ld_acquire_sys(f) - e) < 0) {
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > wait_limit_ns) {
         atomicOr(&g_xm_device_error, XM_DEVERR_TIMEOUT);
         break;
       }
@@ -117,8 +119,10 @@ __global__ void __launch_bounds__(kCommThreads) k_allreduce_add(float* __restric
 struct Comm {
   int world = 0, rank = 0, nctas = 0;
   int64_t max_elems = 0;
+  uint64_t wait_limit_ns = kDefaultWaitLimitNs;
   uint8_t* local = nullptr;            // this rank's buffer (owned)
-  uint8_t* peer[kMaxRanks] = {};       // opened IPC mappings (nullptr for self)
+  uint8_t* peer[kMaxRanks] = {};       // peer buffers: opened IPC mappings or in-process pointers
+  bool ipc[kMaxRanks] = {};            // peer[r] is an IPC mapping (closed on destroy)
 };
 
 }  // namespace
@@ -167,6 +171,27 @@ int xm_comm_open_peer(void* comm, int peer_rank, const void* handle) {
   cudaError_t e = cudaIpcOpenMemHandle(&p, hd, cudaIpcMemLazyEnablePeerAccess);
   if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "comm_open_peer(%d): %s", peer_rank, cudaGetErrorString(e));
   c->peer[peer_rank] = (uint8_t*)p;
+  c->ipc[peer_rank] = true;
+  return XM_OK;
+}
+
+int xm_comm_open_local(void* comm, int peer_rank, void* peer_comm) {
+  Comm* c = (Comm*)comm;
+  Comm* p = (Comm*)peer_comm;
+  if (!c || !p || peer_rank < 0 || peer_rank >= c->world || p->world != c->world || p->rank != peer_rank ||
+      p->max_elems != c->max_elems)
+    return xm_set_error(XM_ERR_INVALID, "comm_open_local: the peer comm must be rank %d of the same shape", peer_rank);
+  if (peer_rank == c->rank) return XM_OK;
+  c->peer[peer_rank] = p->local;
+  c->ipc[peer_rank] = false;
+  return XM_OK;
+}
+
+int xm_comm_set_wait_limit(void* comm, int64_t limit_ns) {
+  Comm* c = (Comm*)comm;
+  if (!c || limit_ns < 1000 || limit_ns > 60000000000ll)
+    return xm_set_error(XM_ERR_INVALID, "comm_set_wait_limit: limit outside 1 us .. 60 s");
+  c->wait_limit_ns = (uint64_t)limit_ns;
   return XM_OK;
 }
 
@@ -175,7 +200,7 @@ int xm_comm_destroy(void* comm) {
   if (!c) return XM_OK;
   cudaError_t first = cudaSuccess;
   for (int r = 0; r < kMaxRanks; ++r)
-    if (c->peer[r]) {
+    if (c->peer[r] && c->ipc[r]) {
       cudaError_t e = cudaIpcCloseMemHandle(c->peer[r]);
       if (first == cudaSuccess) first = e;
     }
@@ -216,7 +241,7 @@ int xm_allreduce_add(void* comm, float* d_h, const float* d_part, int64_t n_elem
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, k_allreduce_add, d_h, d_part, n_elems, c->max_elems, c->world, c->rank,
-                                     t, flags, epochs, recv);
+                                     t, flags, epochs, recv, c->wait_limit_ns);
   if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "allreduce_add launch: %s", cudaGetErrorString(e));
   return xm_check_launch("allreduce_add");
 }

@@ -7,12 +7,17 @@
 
 // Grouped tensor-core GEMM over fp16 activations already prepared (row-scaled):
 // for each group g < G, rows [off[g], off[g] + cnt[g]) of a16 (P x K, fp16)
-// times the Q4_K weight w[g] (N x K) -> y rows (P x N, fp32), scaled back by
-// rowscale.  cnt/off are device arrays, h_w a host array of G <= 32 device
-// pointers; max_rows bounds cnt[g] (grid size).
-int qgemm_q4k_grouped(const __half* a16, const float* rowscale, int64_t P, int64_t K, int64_t N,
-                      const uint8_t* const* h_w, const int* d_cnt, const int* d_off, int G, int64_t max_rows,
-                      int64_t expect_rows, float* y, cudaStream_t st);
+// times the weight w[g] (N x K, GGUF blocks of qtype) -> y rows (P x N, fp32),
+// scaled back by rowscale.  cnt/off are device arrays, h_w a host array of
+// G <= 32 device pointers; max_rows bounds cnt[g] (grid size).
+int qgemm_grouped(int qtype, const __half* a16, const float* rowscale, int64_t P, int64_t K, int64_t N,
+                  const uint8_t* const* h_w, const int* d_cnt, const int* d_off, int G, int64_t max_rows,
+                  int64_t expect_rows, float* y, cudaStream_t st);
+// Whether the tensor-core GEMM takes weights of this type with rows of k
+// elements (k a multiple of 256 and a row a multiple of 16 bytes).
+bool qgemm_type_supported(int qtype, int64_t k);
+// Bytes of one row of k weights of a block type (0: not block-quantized).
+int64_t qgemm_row_bytes(int qtype, int64_t k);
 
 // Generic integer-dot GEMV (Q4_K, Q5_K, Q6_K, Q8_0; k % 128 == 0, k <= 16384)
 // over a group-major activation split in d_ws; y (+)= W x (+ bias).

@@ -18,7 +18,7 @@ namespace {
 constexpr int kHeadDim = 128;
 constexpr int kAttnKeys = 64;    // keys per attention CTA
 constexpr int kMaxGroup = 8;     // query heads per KV head
-constexpr int kMaxLq = 8;        // new tokens per sequence in one call
+constexpr int kMaxLq = 64;       // new tokens per sequence in one call (a prefill chunk)
 
 // ---------------------------------------------------------------------------
 // out[b][:] = fp16-rounded dequantized row ids[b] of a GGUF table (the
@@ -348,7 +348,7 @@ int xm_attention(const float* d_qkv, int64_t qkv_stride, void* d_kcache, void* d
                  int64_t out_stride, void* d_workspace, int64_t workspace_bytes, void* stream) {
   if (head_dim != kHeadDim) return xm_set_error(XM_ERR_UNSUPPORTED, "attention: head_dim %d (only 128)", head_dim);
   if (B < 1 || Lq < 1 || Lq > kMaxLq || Hq < 1 || Hk < 1 || Hq % Hk || Hq / Hk > kMaxGroup)
-    return xm_set_error(XM_ERR_INVALID, "attention: bad head counts (G <= 8) or more than 8 new tokens");
+    return xm_set_error(XM_ERR_INVALID, "attention: bad head counts (G <= 8) or more than %d new tokens", kMaxLq);
   if (max_ctx < 1 || max_ctx > (1 << 24) || qkv_stride < (int64_t)(Hq + 2 * Hk) * kHeadDim ||
       out_stride < (int64_t)Hq * kHeadDim || !d_qkv || !d_kcache || !d_vcache || !d_pos0 || !d_out)
     return xm_set_error(XM_ERR_INVALID, "attention: bad arguments");

@@ -174,8 +174,19 @@ __global__ void __launch_bounds__(256) k_moe_gather(const XT* __restrict__ x, co
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < H; i += gridDim.x * blockDim.x) o[i] = xr[i];
 }
 
-// silu(g) * u (primitives.py:37-44: x / (1 + exp(-x)) times up), then the
-// fp16 row preparation of the down projection's activation.
+// act(g) * u, then the fp16 row preparation of the down projection's
+// activation.  act is the reference's apply_activation (primitives.py:37-62):
+// silu x / (1 + exp(-x)), gelu (tanh form) 0.5 x (1 + tanh(0.7978845608 (x +
+// 0.044715 x^3))), relu max(x, 0), identity.
+template <int ACT>
+XM_DEV float expert_act(float x) {
+  if constexpr (ACT == XM_ACT_SILU) return x / (1.0f + expf(-x));
+  else if constexpr (ACT == XM_ACT_GELU) return 0.5f * x * (1.0f + tanhf(0.7978845608f * (x + 0.044715f * x * x * x)));
+  else if constexpr (ACT == XM_ACT_RELU) return fmaxf(x, 0.0f);
+  else return x;
+}
+
+template <int ACT>
 __global__ void __launch_bounds__(256) k_swiglu_prep(const float* __restrict__ g, const float* __restrict__ u, int P,
                                                      int F, __half* __restrict__ h16, float* __restrict__ hscale) {
   const int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -183,10 +194,7 @@ __global__ void __launch_bounds__(256) k_swiglu_prep(const float* __restrict__ g
   const float* gr = g + (int64_t)p * F;
   const float* ur = u + (int64_t)p * F;
   float amax = 0.f;
-  for (int i = lane; i < F; i += 32) {
-    const float gv = gr[i];
-    amax = fmaxf(amax, fabsf(gv / (1.0f + expf(-gv)) * ur[i]));
-  }
+  for (int i = lane; i < F; i += 32) amax = fmaxf(amax, fabsf(expert_act<ACT>(gr[i]) * ur[i]));
 #pragma unroll
   for (int s = 16; s > 0; s >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, s));
   int sh = 0;
@@ -197,10 +205,7 @@ __global__ void __launch_bounds__(256) k_swiglu_prep(const float* __restrict__ g
   }
   const float inv = ldexpf(1.0f, -sh);
   __half* o = h16 + (int64_t)p * F;
-  for (int i = lane; i < F; i += 32) {
-    const float gv = gr[i];
-    o[i] = __float2half_rn(gv / (1.0f + expf(-gv)) * ur[i] * inv);
-  }
+  for (int i = lane; i < F; i += 32) o[i] = __float2half_rn(expert_act<ACT>(gr[i]) * ur[i] * inv);
   if (lane == 0) hscale[p] = ldexpf(1.0f, sh);
 }
 
@@ -304,17 +309,37 @@ int route_and_sort(const void* d_x, int x_dtype, int64_t T, int64_t H, const flo
 // prepared fp16 rows a16 (P x H, already in expert order) -> d (P x H): the
 // SwiGLU experts of G groups (rows [off[g], off[g] + cnt[g]) use weights tab[g],
 // tab[G + g], tab[2G + g] for w1, w3, w2)
-int run_experts(const __half* a16, const float* ascale, int64_t P, int64_t H, int64_t F, const uint8_t* const* tab,
-                int G, const int* cnt, const int* off, int64_t max_rows, float* g, float* u, __half* h16,
-                float* hscale, float* d, cudaStream_t st) {
+int run_experts(int qtype, int act, const __half* a16, const float* ascale, int64_t P, int64_t H, int64_t F,
+                const uint8_t* const* tab, int G, const int* cnt, const int* off, int64_t max_rows, float* g,
+                float* u, __half* h16, float* hscale, float* d, cudaStream_t st) {
   const int64_t expect = std::max<int64_t>(1, P / G);
   int rc;
-  if ((rc = qgemm_q4k_grouped(a16, ascale, P, H, F, tab, cnt, off, G, max_rows, expect, g, st))) return rc;
-  if ((rc = qgemm_q4k_grouped(a16, ascale, P, H, F, tab + G, cnt, off, G, max_rows, expect, u, st))) return rc;
+  if ((rc = qgemm_grouped(qtype, a16, ascale, P, H, F, tab, cnt, off, G, max_rows, expect, g, st))) return rc;
+  if ((rc = qgemm_grouped(qtype, a16, ascale, P, H, F, tab + G, cnt, off, G, max_rows, expect, u, st))) return rc;
   const unsigned pgrid = (unsigned)((P * 32 + 255) / 256);
-  k_swiglu_prep<<<pgrid, 256, 0, st>>>(g, u, (int)P, (int)F, h16, hscale);
+  if (act == XM_ACT_SILU)
+    k_swiglu_prep<XM_ACT_SILU><<<pgrid, 256, 0, st>>>(g, u, (int)P, (int)F, h16, hscale);
+  else if (act == XM_ACT_GELU)
+    k_swiglu_prep<XM_ACT_GELU><<<pgrid, 256, 0, st>>>(g, u, (int)P, (int)F, h16, hscale);
+  else if (act == XM_ACT_RELU)
+    k_swiglu_prep<XM_ACT_RELU><<<pgrid, 256, 0, st>>>(g, u, (int)P, (int)F, h16, hscale);
+  else
+    k_swiglu_prep<XM_ACT_IDENTITY><<<pgrid, 256, 0, st>>>(g, u, (int)P, (int)F, h16, hscale);
   if ((rc = xm_check_launch("moe swiglu"))) return rc;
-  return qgemm_q4k_grouped(h16, hscale, P, F, H, tab + 2 * G, cnt, off, G, max_rows, expect, d, st);
+  return qgemm_grouped(qtype, h16, hscale, P, F, H, tab + 2 * G, cnt, off, G, max_rows, expect, d, st);
+}
+
+// Expert weights of this type and shape have a tensor-core path, and the
+// activation is one the reference knows.
+int check_expert_type(const char* who, int qtype, int act, int64_t H, int64_t F) {
+  if (act != XM_ACT_SILU && act != XM_ACT_GELU && act != XM_ACT_RELU && act != XM_ACT_IDENTITY)
+    return xm_set_error(XM_ERR_INVALID, "%s: unknown activation %d", who, act);
+  if (!qgemm_type_supported(qtype, H) || !qgemm_type_supported(qtype, F))
+    return xm_set_error(XM_ERR_UNSUPPORTED,
+                        "%s: expert type id %d with hidden %lld / intermediate %lld has no tensor-core path (block "
+                        "type with rows of whole 16-byte units needed)",
+                        who, qtype, (long long)H, (long long)F);
+  return XM_OK;
 }
 
 struct ExpertWs {
@@ -341,11 +366,11 @@ ExpertWs carve_experts(uint8_t* base, int64_t P, int64_t H, int64_t F) {
 
 extern "C" int xm_moe_forward(const void* d_x, int x_dtype, int64_t T, int64_t H, const float* d_gate, int E, int k,
                               int64_t F, const void* const* h_w1, const void* const* h_w3, const void* const* h_w2,
-                              int qtype, float* d_out, void* d_ws, int64_t ws_bytes, void* stream) {
-  if (qtype != T_Q4_K) return xm_set_error(XM_ERR_UNSUPPORTED, "moe: expert type id %d has no tensor-core path", qtype);
+                              int qtype, int activation, float* d_out, void* d_ws, int64_t ws_bytes, void* stream) {
   if (int rc0 = check_common(E, k, T, H, x_dtype)) return rc0;
   if (F < 256 || F % 256)
     return xm_set_error(XM_ERR_INVALID, "moe: hidden and intermediate sizes must be positive multiples of 256");
+  if (int rc0 = check_expert_type("moe", qtype, activation, H, F)) return rc0;
   if (!d_x || !d_gate || !d_out || !d_ws || !h_w1 || !h_w2 || !h_w3)
     return xm_set_error(XM_ERR_INVALID, "moe: null pointer");
   if (((uintptr_t)d_ws & 255) || ws_bytes < xm_moe_workspace_size(T, H, F, E, k))
@@ -376,7 +401,8 @@ extern "C" int xm_moe_forward(const void* d_x, int x_dtype, int64_t T, int64_t H
   else
     k_moe_gather_prep<__half><<<pgrid, 256, 0, st>>>((const __half*)d_x, w.sorted_tok, (int)P, (int)H, w.a16, w.ascale);
   if ((rc = xm_check_launch("moe gather"))) return rc;
-  if ((rc = run_experts(w.a16, w.ascale, P, H, F, tab, E, w.cnt, w.off, T, w.g, w.u, w.h16, w.hscale, w.d, st)))
+  if ((rc = run_experts(qtype, activation, w.a16, w.ascale, P, H, F, tab, E, w.cnt, w.off, T, w.g, w.u, w.h16, w.hscale, w.d,
+                       st)))
     return rc;
   const unsigned tgrid = (unsigned)((T * 32 + 255) / 256);
   k_moe_combine<<<tgrid, 256, 0, st>>>(w.d, w.topk_e, w.topk_w, w.pair_pos, (int)T, (int)H, k, d_out);
@@ -418,12 +444,13 @@ extern "C" int64_t xm_moe_experts_workspace_size(int64_t P, int64_t H, int64_t F
 
 extern "C" int xm_moe_experts(const void* d_rows, int x_dtype, int64_t P, int64_t H, int64_t F, int G, const int* d_cnt,
                               const int* d_off, const void* const* h_w1, const void* const* h_w3,
-                              const void* const* h_w2, int qtype, int64_t max_rows, float* d_out, void* d_ws,
+                              const void* const* h_w2, int qtype, int activation, int64_t max_rows, float* d_out,
+                              void* d_ws,
                               int64_t ws_bytes, void* stream) {
-  if (qtype != T_Q4_K) return xm_set_error(XM_ERR_UNSUPPORTED, "moe_experts: expert type id %d has no tensor-core path", qtype);
   if (G < 1 || G > kMaxExperts) return xm_set_error(XM_ERR_INVALID, "moe_experts: %d groups (1..%d)", G, kMaxExperts);
   if (P < 0 || H < 256 || H % 256 || F < 256 || F % 256 || max_rows < 0)
     return xm_set_error(XM_ERR_INVALID, "moe_experts: bad sizes");
+  if (int rc0 = check_expert_type("moe_experts", qtype, activation, H, F)) return rc0;
   if (x_dtype != XM_DT_F32 && x_dtype != XM_DT_BF16 && x_dtype != XM_DT_F16)
     return xm_set_error(XM_ERR_INVALID, "moe_experts: bad x dtype %d", x_dtype);
   if (P == 0) return XM_OK;
@@ -452,8 +479,8 @@ extern "C" int xm_moe_experts(const void* d_rows, int x_dtype, int64_t P, int64_
     k_moe_gather_prep<__half><<<pgrid, 256, 0, st>>>((const __half*)d_rows, nullptr, (int)P, (int)H, w.a16, w.ascale);
   int rc = xm_check_launch("moe_experts prep");
   if (rc) return rc;
-  return run_experts(w.a16, w.ascale, P, H, F, tab, G, d_cnt, d_off, std::max<int64_t>(1, max_rows), w.g, w.u, w.h16,
-                     w.hscale, d_out, st);
+  return run_experts(qtype, activation, w.a16, w.ascale, P, H, F, tab, G, d_cnt, d_off, std::max<int64_t>(1, max_rows), w.g, w.u,
+                     w.h16, w.hscale, d_out, st);
 }
 
 extern "C" int xm_moe_combine(const float* d_rows, int64_t T, int64_t H, int E, int k, int64_t F, const void* d_ws,

@@ -1,9 +1,11 @@
 // K3: fused dequant-GEMM for prefill on 5th-generation tensor cores.
 //
-//   y[m][n] = sum_k x[m][k] * W[n][k]   (fp32 out), W in GGUF Q4_K blocks.
+//   y[m][n] = sum_k x[m][k] * W[n][k]   (fp32 out), W in GGUF blocks of any
+//   of the twelve block-quantized types (Q4_0 ... Q8_K).
 //
 // Numerics.  Every weight is decoded to the reference's fp16 value (the fp32
-// value d*sc*q - dmin*mn rounded once to fp16), so B is exact.  The
+// value of gguf_dequant.py's unpacker, e.g. d*sc*q - dmin*mn for Q4_K,
+// rounded once to fp16), so B is exact.  The
 // activation is converted to fp16 after scaling each row by a power of two
 // chosen from the row's largest magnitude (k_prep_rows): bf16 input converts
 // exactly, and the scale keeps rows with large or tiny values inside fp16's
@@ -14,13 +16,13 @@
 // rounding).
 //
 // Two kernels:
-//  * k_qgemm_q4k_pair (the default): persistent CTA pairs on tcgen05
-//    cta_group::2 (M = 256 per MMA), raw Q4_K records staged by TMA and decoded
-//    by two interleaved groups of decode warps, double-buffered TMEM
-//    accumulators with dedicated epilogue warps; dense and grouped (MoE)
-//    modes.  Its own comment block below has the details.
-//  * k_qgemm_q4k_tc: one CTA per output tile of MT*128 rows x BN columns, used
-//    when a device cannot hold a CTA pair of the chosen size:
+//  * k_qgemm_pair<T> (the default, every block type T): persistent CTA pairs
+//    on tcgen05 cta_group::2 (M = 256 per MMA), raw block records staged by
+//    TMA and decoded by two interleaved groups of decode warps,
+//    double-buffered TMEM accumulators with dedicated epilogue warps; dense
+//    and grouped (MoE) modes.  Its own comment block below has the details.
+//  * k_qgemm_q4k_tc (Q4_K only): one CTA per output tile of MT*128 rows x BN
+//    columns, used when a device cannot hold a CTA pair of the chosen size:
 //   warp 0      TMA producer of the activation tiles (fp16, 128-byte swizzle,
 //               2-D tensor map, no multicast).
 //   warp 1      allocates tensor memory and issues tcgen05.mma (one thread).
@@ -120,18 +122,44 @@ XM_DEV float byte_f(uint32_t w, int i) {
 }
 
 // ---------------------------------------------------------------------------
-// Activation preparation: fp16 copy of x with a power-of-two scale per row.
-// One warp per row.  rowscale[m] = 2^s with the row's max magnitude in
+// Activation preparation: fp16 copy of pro(x) with a power-of-two scale per
+// row.  One warp per row.  rowscale[m] = 2^s with the row's max magnitude in
 // [2^14, 2^15) after division by 2^s (s may be negative for small rows).
+// PRO is an XM_PRO_* prologue, applied in fp32 in the reference's order:
+//   XM_PRO_RMSNORM  v = (x / sqrt(mean(x^2) + eps)) * norm_w   (ops.py:115-117)
+//   XM_PRO_SWIGLU   v = silu(x[:K]) * x[K:2K]                  (forward.py:97-98)
+// `ldx` is the row pitch of x in elements.
 // ---------------------------------------------------------------------------
-template <typename XT>
-__global__ void __launch_bounds__(256) k_prep_rows(const XT* __restrict__ x, int M, int K, __half* __restrict__ x16,
-                                                   float* __restrict__ rowscale) {
+template <typename XT, int PRO>
+XM_DEV float prep_value(const XT* xr, int k, int K, float rms, const float* norm_w) {
+  if constexpr (PRO == XM_PRO_RMSNORM) {
+    return (to_f32(xr[k]) / rms) * norm_w[k];
+  } else if constexpr (PRO == XM_PRO_SWIGLU) {
+    const float g = to_f32(xr[k]);
+    return g / (1.0f + expf(-g)) * to_f32(xr[K + k]);
+  } else {
+    return to_f32(xr[k]);
+  }
+}
+
+template <typename XT, int PRO>
+__global__ void __launch_bounds__(256) k_prep_rows(const XT* __restrict__ x, int M, int K, int64_t ldx,
+                                                   const float* __restrict__ norm_w, float eps,
+                                                   __half* __restrict__ x16, float* __restrict__ rowscale) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= M) return;
-  const XT* xr = x + (int64_t)warp * K;
+  const XT* xr = x + (int64_t)warp * ldx;
+  float rms = 1.f;
+  if constexpr (PRO == XM_PRO_RMSNORM) {
+    float ss = 0.f;
+    for (int k = lane; k < K; k += 32) {
+      const float v = to_f32(xr[k]);
+      ss = fmaf(v, v, ss);
+    }
+    rms = sqrtf(warp_sum(ss) / (float)K + eps);
+  }
   float amax = 0.f;
-  for (int k = lane; k < K; k += 32) amax = fmaxf(amax, fabsf(to_f32(xr[k])));
+  for (int k = lane; k < K; k += 32) amax = fmaxf(amax, fabsf(prep_value<XT, PRO>(xr, k, K, rms, norm_w)));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   int s = 0;
@@ -142,8 +170,27 @@ __global__ void __launch_bounds__(256) k_prep_rows(const XT* __restrict__ x, int
   }
   const float inv = ldexpf(1.0f, -s);
   __half* o = x16 + (int64_t)warp * K;
-  for (int k = lane; k < K; k += 32) o[k] = __float2half_rn(to_f32(xr[k]) * inv);
+  for (int k = lane; k < K; k += 32) o[k] = __float2half_rn(prep_value<XT, PRO>(xr, k, K, rms, norm_w) * inv);
   if (lane == 0) rowscale[warp] = ldexpf(1.0f, s);
+}
+
+// Plain RMSNorm of rows (one warp per row), fp32 out: the norm of
+// FusedRMSNormLinearOp for weights whose matmul has no fused prologue.
+template <typename XT>
+__global__ void __launch_bounds__(256) k_rmsnorm_rows(const XT* __restrict__ x, int M, int K, int64_t ldx,
+                                                      const float* __restrict__ norm_w, float eps,
+                                                      float* __restrict__ out) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= M) return;
+  const XT* xr = x + (int64_t)warp * ldx;
+  float ss = 0.f;
+  for (int k = lane; k < K; k += 32) {
+    const float v = to_f32(xr[k]);
+    ss = fmaf(v, v, ss);
+  }
+  const float rms = sqrtf(warp_sum(ss) / (float)K + eps);
+  float* o = out + (int64_t)warp * K;
+  for (int k = lane; k < K; k += 32) o[k] = (to_f32(xr[k]) / rms) * norm_w[k];
 }
 
 // ---------------------------------------------------------------------------
@@ -232,7 +279,7 @@ XM_DEV void decode_item(const RawItem& it, int h, int j, uint8_t* row, int n) {
 __global__ void __launch_bounds__(kThreads, 1)
     k_qgemm_q4k_tc(const __grid_constant__ CUtensorMap map_a, const uint8_t* __restrict__ W0, int M, int N,
                    int K, int MT, int BN, int kStages, const float* __restrict__ rowscale,
-                   const float* __restrict__ bias, float* __restrict__ y, GemmGroups groups) {
+                   const float* __restrict__ bias, float* __restrict__ y, int acc, GemmGroups groups) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte aligned carve-up: A stages | B stages | control
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -370,7 +417,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float bv = (bias && nn < N) ? bias[nn] : 0.f;
         for (int r = 0; r < 32; ++r) {
           const int m = mrow0 + r;
-          if (m < mhi && nn < N) y[(int64_t)m * N + nn] = tile[r * 33 + lane] + bv;
+          if (m < mhi && nn < N) {
+            float* yp = y + (int64_t)m * N + nn;
+            const float o = tile[r * 33 + lane] + bv;
+            *yp = acc ? *yp + o : o;
+          }
         }
         __syncwarp();
       }
@@ -396,12 +447,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 // pairs (order: pair_tile).
 //
 // Per CTA (2 + 16 + 4 warps):
-//   warp 0      TMA producer: raw Q4_K records of the CTA's weight rows, one
-//               256-wide super-block column per stage (box 144 B x BN/2 rows,
-//               per N half), and the fp16 activation box (64 K x 128 rows,
-//               128-byte swizzle) of every 64-wide K step.  Rank 1's
-//               activation box completes on rank 0's barrier (cta_group::2
-//               form of the tensor load; no multicast).
+//   warp 0      TMA producer: raw block records of the CTA's weight rows, one
+//               256-wide K column per stage (ColGeom<T>: a box of BB bytes x
+//               BN/2 rows per N half, starting at the column's first byte
+//               rounded down to 16 -- TMA's alignment rule -- and wide enough
+//               for the column at any of its offsets), and the fp16
+//               activation box (64 K x 128 rows, 128-byte swizzle) of every
+//               64-wide K step.  Rank 1's activation box completes on rank 0's
+//               barrier (cta_group::2 form of the tensor load; no multicast).
 //   warp 1      TMEM allocation (both ranks); rank 0 issues the MMAs.
 //   warps 2-17  decode, two groups of 8 warps taking turns by K step: one
 //               thread per (row, 32-weight sub-block) item, from the staged
@@ -427,8 +480,47 @@ __global__ void __launch_bounds__(kThreads, 1)
 constexpr int kPairEpiWarps = 4;
 constexpr int pair_threads(int dw) { return (2 + dw + kPairEpiWarps) * 32; }
 constexpr int kMaxRawStages = 2;
-constexpr int kRecBytes = 144;                 // one Q4_K super-block record
 constexpr int kEpiTileFloats = 32 * 33;        // per-warp padded 32 x 32 staging tile
+
+// Staging geometry of one 256-wide K column of a weight row of type T: CB
+// bytes in the row (one Q4_K record; eight Q8_0 records; ...).  Column kb
+// starts at byte kb*CB of its row, which is 16-byte aligned only when CB is a
+// multiple of 16; its offset inside the 16-byte unit is a multiple of
+// gcd(CB, 16), at most MIS.  The TMA box (BB bytes per row, 16-bit elements)
+// starts at the rounded-down address and covers CB + MIS bytes.
+constexpr int gcd16(int v) { return (v & 15) == 0 ? 16 : (v & 7) == 0 ? 8 : (v & 3) == 0 ? 4 : (v & 1) == 0 ? 2 : 1; }
+template <int T>
+struct ColGeom {
+  static constexpr int QK = QT<T>::QK, REC = QT<T>::REC;
+  static constexpr int CB = REC * (256 / QK);
+  static constexpr int MIS = (CB & 15) == 0 ? 0 : 16 - gcd16(CB);
+  static constexpr int BB = (CB + MIS + 15) / 16 * 16;
+  static_assert(BB / 2 <= 256, "TMA box width");
+};
+
+// One decode item of a type without a hand-tuned decoder: weights 32h .. 32h+31
+// of K step j (64 weights) of one row, from the staged column `col`, rounded
+// to fp16 (the reference's values) and stored as four 16-byte chunks into the
+// swizzled B row (n: the row's index for the swizzle pattern).
+template <int T>
+XM_DEV void decode_item_generic(const uint8_t* col, int j, int h, uint8_t* row, int n) {
+  using Q = QT<T>;
+  const uint8_t* rec = Q::QK == 256 ? col : col + (2 * j + h) * Q::REC;
+  const int e0 = Q::QK == 256 ? 64 * j + 32 * h : 0;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    float v[8];
+    Q::decode8(rec, e0 + 8 * c, v);
+    uint32_t hv[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const __half2 hh = __floats2half2_rn(v[2 * p], v[2 * p + 1]);
+      hv[p] = *reinterpret_cast<const uint32_t*>(&hh);
+    }
+    const int chunk = 4 * h + c;
+    *reinterpret_cast<uint4*>(row + ((chunk ^ (n & 7)) << 4)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+  }
+}
 
 struct PairSmem {
   uint64_t wfull[kMaxRawStages], wempty[kMaxRawStages];
@@ -548,18 +640,19 @@ XM_DEV bool pair_tile(const PairW<NMAP>& pw, int t, int M, int TM, int TN, int w
 // NH = 1: tile 256 x BN, two accumulators (the epilogue of one tile overlaps
 // the main loop of the next).  NH = 2: tile 256 x 2BN as two N = BN MMAs into
 // one accumulator of 2BN columns (fewer, wider tiles for mid-size M).
-template <int DW, int NMAP>
+template <int T, int DW, int NMAP>
 __global__ void __launch_bounds__(pair_threads(DW), 1)
-    k_qgemm_q4k_pair(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ PairW<NMAP> pw, int M,
-                     int N, int K, int BN, int NH, int S, int RW, int TM, const float* __restrict__ rowscale,
-                     const float* __restrict__ bias, float* __restrict__ y) {
+    k_qgemm_pair(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ PairW<NMAP> pw, int M, int N,
+                 int K, int BN, int NH, int S, int RW, int TM, const float* __restrict__ rowscale,
+                 const float* __restrict__ bias, float* __restrict__ y, int acc) {
+  using CG = ColGeom<T>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int hb = BN >> 1;                         // rows of each N half this CTA decodes
   const int rows = NH * hb;                       // weight rows decoded by this CTA per K step
   const int width = NH * BN;                      // output columns of a tile
   const int ostage = kATileBytes + rows * 128;    // [A 128 x 64 fp16 | B half 0 | B half 1], 1024-byte multiples
-  const int wstage = rows * kRecBytes;            // the CTA's records of one super-block column
+  const int wstage = rows * CG::BB;               // the CTA's staged bytes of one 256-wide K column
   uint8_t* sO = base;
   uint8_t* sW = sO + S * ostage;
   float* sEpi = reinterpret_cast<float*>(sW + RW * wstage);
@@ -569,7 +662,7 @@ __global__ void __launch_bounds__(pair_threads(DW), 1)
   const uint32_t rank = cluster_ctarank();
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int TN = (N + width - 1) / width;
-  const int T = TM * TN * (NMAP == 1 ? 1 : pw.groups);
+  const int NT = TM * TN * (NMAP == 1 ? 1 : pw.groups);   // tiles
   const int KB = K >> 8, nkt = K / kBK;
   const int nacc = NH == 1 ? 2 : 1;               // accumulators of `width` columns in TMEM
 
@@ -611,7 +704,7 @@ __global__ void __launch_bounds__(pair_threads(DW), 1)
       grid_dep_wait();
       const uint32_t leader_ofull = mapa_shared(smem_u32(&ctl->ofull[0]), 0);
       uint32_t s = 0, ph = 0, rs = 0, rph = 0;
-      for (int t = pair; t < T; t += npairs) {
+      for (int t = pair; t < NT; t += npairs) {
         PairTile pt;
         if (!pair_tile(pw, t, M, TM, TN, width, pt)) continue;
         const CUtensorMap* wmap = &pw.map[NMAP == 1 ? 0 : pt.g];
@@ -620,8 +713,9 @@ __global__ void __launch_bounds__(pair_threads(DW), 1)
         for (int kb = 0; kb < KB; ++kb) {
           pair_wait(&ctl->wempty[rs], rph ^ 1);
           mbar_arrive_expect_tx(&ctl->wfull[rs], (uint32_t)wstage);
+          const int wx = ((kb * CG::CB) & ~15) >> 1;   // 16-byte aligned start, in 16-bit elements
           for (int h = 0; h < NH; ++h)
-            tma_load_2d(sW + rs * wstage + h * hb * kRecBytes, wmap, kb * kRecBytes, wn + h * BN, &ctl->wfull[rs]);
+            tma_load_2d(sW + rs * wstage + h * hb * CG::BB, wmap, wx, wn + h * BN, &ctl->wfull[rs]);
           if (++rs == (uint32_t)RW) { rs = 0; rph ^= 1; }
           for (int j = 0; j < 4; ++j, ka += kBK) {
             pair_wait(&ctl->oempty[s], ph ^ 1);
@@ -645,7 +739,7 @@ __global__ void __launch_bounds__(pair_threads(DW), 1)
       const uint64_t step = (uint64_t)(ostage >> 4), bhalf = (uint64_t)((hb * 128) >> 4);
       uint32_t s = 0, ph = 0, it = 0;
       uint64_t off = 0;
-      for (int t = pair; t < T; t += npairs) {
+      for (int t = pair; t < NT; t += npairs) {
         PairTile pt;
         if (!pair_tile(pw, t, M, TM, TN, width, pt)) continue;
         const uint32_t b = nacc == 2 ? (it & 1) : 0u, u = nacc == 2 ? (it >> 1) : it;
@@ -681,16 +775,19 @@ __global__ void __launch_bounds__(pair_threads(DW), 1)
     const int h = dt & 1, n = dt >> 1;
     const uint32_t leader_ofull = mapa_shared(smem_u32(&ctl->ofull[0]), 0);
     uint32_t s = (uint32_t)grp, ph = 0, rs = 0, rph = 0;   // this group's first step is q = grp (< S)
-    for (int t = pair; t < T; t += npairs) {
+    for (int t = pair; t < NT; t += npairs) {
       PairTile pt;
       if (!pair_tile(pw, t, M, TM, TN, width, pt)) continue;
       for (int kb = 0; kb < KB; ++kb) {
         pair_wait(&ctl->wfull[rs], rph);
-        uint4 hd[2];
+        const int mis = (kb * CG::CB) & 15;       // the column's offset in its staged box (0 for Q4_K)
+        [[maybe_unused]] uint4 hd[2];
+        if constexpr (T == T_Q4_K) {
 #pragma unroll
-        for (int p = 0; p < 2; ++p) {
-          const int rl = p * 128 + n;
-          if (rl < rows) hd[p] = *reinterpret_cast<const uint4*>(sW + rs * wstage + rl * kRecBytes);
+          for (int p = 0; p < 2; ++p) {
+            const int rl = p * 128 + n;
+            if (rl < rows) hd[p] = *reinterpret_cast<const uint4*>(sW + rs * wstage + rl * CG::BB);
+          }
         }
         for (int j = grp; j < 4; j += kGroups) {
           pair_wait(&ctl->oempty[s], ph ^ 1);
@@ -699,11 +796,16 @@ __global__ void __launch_bounds__(pair_threads(DW), 1)
             const int rl = p * 128 + n;
             if (rl < rows) {
               const int half = rl >= hb ? 1 : 0, rr = rl - half * hb;
-              const uint8_t* rec = sW + rs * wstage + rl * kRecBytes;
-              const uint4 q0 = *reinterpret_cast<const uint4*>(rec + 16 + 32 * j);
-              const uint4 q1 = *reinterpret_cast<const uint4*>(rec + 32 + 32 * j);
-              const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-              decode_part<4>(hd[p], qw, h, j, 0, sO + s * ostage + kATileBytes + half * hb * 128 + rr * 128, rr);
+              const uint8_t* rec = sW + rs * wstage + rl * CG::BB + mis;
+              uint8_t* dst = sO + s * ostage + kATileBytes + half * hb * 128 + rr * 128;
+              if constexpr (T == T_Q4_K) {
+                const uint4 q0 = *reinterpret_cast<const uint4*>(rec + 16 + 32 * j);
+                const uint4 q1 = *reinterpret_cast<const uint4*>(rec + 32 + 32 * j);
+                const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+                decode_part<4>(hd[p], qw, h, j, 0, dst, rr);
+              } else {
+                decode_item_generic<T>(rec, j, h, dst, rr);
+              }
             }
           }
           fence_proxy_async_smem();               // generic-proxy writes -> visible to the tensor core
@@ -730,7 +832,7 @@ __global__ void __launch_bounds__(pair_threads(DW), 1)
     float* tile = sEpi + ew * kEpiTileFloats;
     const uint32_t leader_acc_empty = mapa_shared(smem_u32(&ctl->acc_empty[0]), 0);
     uint32_t it = 0;
-    for (int t = pair; t < T; t += npairs) {
+    for (int t = pair; t < NT; t += npairs) {
       PairTile pt;
       if (!pair_tile(pw, t, M, TM, TN, width, pt)) continue;
       const uint32_t b = nacc == 2 ? (it & 1) : 0u, u = nacc == 2 ? (it >> 1) : it;
@@ -749,7 +851,11 @@ __global__ void __launch_bounds__(pair_threads(DW), 1)
         const float bv = (bias && nn < N) ? bias[nn] : 0.f;
         for (int r = 0; r < 32; ++r) {
           const int m = mrow0 + r;
-          if (m < pt.mhi && nn < N) y[(int64_t)m * N + nn] = tile[r * 33 + lane] + bv;
+          if (m < pt.mhi && nn < N) {
+            float* yp = y + (int64_t)m * N + nn;
+            const float o = tile[r * 33 + lane] + bv;
+            *yp = acc ? *yp + o : o;
+          }
         }
         __syncwarp();
       }
@@ -841,7 +947,7 @@ int encode_a16(CUtensorMap* map, const __half* a16, int64_t rows, int64_t k) {
 }
 
 int launch_gemm(const CUtensorMap& map_a, const uint8_t* w, int64_t m, int64_t n, int64_t k, TileCfg cfg,
-                dim3 grid, const float* rowscale, const float* bias, float* y, const GemmGroups& groups,
+                dim3 grid, const float* rowscale, const float* bias, float* y, int acc, const GemmGroups& groups,
                 cudaStream_t st) {
   const int smem = 1024 + cfg.stages * (cfg.MT * kATileBytes + cfg.BN * kBK * 2) + (int)sizeof(GemmSmem);
   cudaError_t e = cudaFuncSetAttribute(k_qgemm_q4k_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -857,7 +963,7 @@ int launch_gemm(const CUtensorMap& map_a, const uint8_t* w, int64_t m, int64_t n
   lc.attrs = attr;
   lc.numAttrs = 1;
   e = cudaLaunchKernelEx(&lc, k_qgemm_q4k_tc, map_a, w, (int)m, (int)n, (int)k, cfg.MT, cfg.BN, cfg.stages, rowscale,
-                         bias, y, groups);
+                         bias, y, acc, groups);
   if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemm launch: %s", cudaGetErrorString(e));
   return xm_check_launch("qgemm");
 }
@@ -874,36 +980,45 @@ struct PairCfg {
   int BN, NH, S, RW, smem;
 };
 
-int pair_smem_bytes(int BN, int NH, int S, int RW) {
+int pair_smem_bytes(int BN, int NH, int S, int RW, int BB) {
   const int rows = NH * (BN / 2);
-  return 1024 + S * (kATileBytes + rows * 128) + RW * rows * kRecBytes + kPairEpiWarps * kEpiTileFloats * 4 +
+  return 1024 + S * (kATileBytes + rows * 128) + RW * rows * BB + kPairEpiWarps * kEpiTileFloats * 4 +
          (int)sizeof(PairSmem);
 }
 
 // Deepest operand ring that fits; S = 0 if fewer than 3 stages fit.
-PairCfg pair_stages(int BN, int NH) {
+PairCfg pair_stages(int BN, int NH, int BB) {
   int S = kMaxStages;
-  while (S > 2 && pair_smem_bytes(BN, NH, S, kPairRaw) > 227 * 1024) --S;
+  while (S > 2 && pair_smem_bytes(BN, NH, S, kPairRaw, BB) > 227 * 1024) --S;
   if (S < 3) S = 0;
-  return {BN, NH, S, kPairRaw, pair_smem_bytes(BN, NH, S, kPairRaw)};
+  return {BN, NH, S, kPairRaw, pair_smem_bytes(BN, NH, S, kPairRaw, BB)};
 }
 
-template <int NMAP>
+template <int T, int NMAP>
 const void* pair_kernel() {
-  return reinterpret_cast<const void*>(k_qgemm_q4k_pair<kPairDW, NMAP>);
+  return reinterpret_cast<const void*>(k_qgemm_pair<T, kPairDW, NMAP>);
 }
 
-// How many CTA pairs of a configuration can be resident at once (0 if the
-// device cannot launch the pair kernel); cached per device and configuration.
-int pair_capacity(const PairCfg& cfg) {
-  static int cache[16][2][9];
-  static bool known[16][2][9];
+// How many CTA pairs of a kernel and shared-memory size can be resident at
+// once (0 if the device cannot launch it); cached per device, kernel and size.
+int pair_capacity(const void* fn, const PairCfg& cfg) {
+  struct Key {
+    int dev;
+    const void* fn;
+    int smem;
+  };
+  static std::mutex mu;
+  static Key keys[256];
+  static int vals[256];
+  static int used = 0;
   int dev = 0;
   cudaGetDevice(&dev);
-  const int a = cfg.NH - 1, b = cfg.BN / 32;
-  if (dev >= 0 && dev < 16 && known[dev][a][b]) return cache[dev][a][b];
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < used; ++i)
+      if (keys[i].dev == dev && keys[i].fn == fn && keys[i].smem == cfg.smem) return vals[i];
+  }
   int n = 0;
-  const void* fn = pair_kernel<1>();
   if (cfg.S >= 3 && cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, cfg.smem) == cudaSuccess) {
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3(2);
@@ -919,9 +1034,11 @@ int pair_capacity(const PairCfg& cfg) {
     if (cudaOccupancyMaxActiveClusters(&n, fn, &lc) != cudaSuccess) n = 0;
   }
   cudaGetLastError();
-  if (dev >= 0 && dev < 16) {
-    cache[dev][a][b] = n;
-    known[dev][a][b] = true;
+  std::lock_guard<std::mutex> lock(mu);
+  if (used < 256) {
+    keys[used] = Key{dev, fn, cfg.smem};
+    vals[used] = n;
+    ++used;
   }
   return n;
 }
@@ -930,14 +1047,14 @@ int pair_capacity(const PairCfg& cfg) {
 // <= 256) and NH (1: double-buffered accumulators; 2: one accumulator of 2BN
 // columns).  Estimated time per pair: rounds x main loop (MMA per K step plus
 // a fixed cost) plus the epilogues that do not overlap.
-PairCfg choose_pair(int64_t mtiles, int64_t n, int64_t k, int pairs) {
+PairCfg choose_pair(int64_t mtiles, int64_t n, int64_t k, int pairs, int BB) {
   PairCfg best{0, 0, 0, 0, 0};
   double best_t = 1e30;
   const double nkt = (double)(k / kBK);
   for (int nh = 1; nh <= 2; ++nh)
     for (int bn = 256; bn >= 32; bn -= 32) {
       if (nh == 2 && bn < 128) continue;
-      const PairCfg c = pair_stages(bn, nh);
+      const PairCfg c = pair_stages(bn, nh, BB);
       if (c.S < 3) continue;
       const int width = nh * bn;
       const int64_t tiles = mtiles * ((n + width - 1) / width);
@@ -953,25 +1070,34 @@ PairCfg choose_pair(int64_t mtiles, int64_t n, int64_t k, int pairs) {
   return best;
 }
 
+// Bytes of one weight row of type T (k a multiple of 256).  The pair kernel
+// moves rows with a 2-D tensor map, whose row pitch must be a multiple of 16.
+template <int T>
+int64_t pair_row_bytes(int64_t k) {
+  return (k / 256) * ColGeom<T>::CB;
+}
+
+template <int T>
 int encode_w_records(CUtensorMap* map, const uint8_t* w, int64_t n, int64_t k, int rows_per_box) {
   EncodeTiledFn encode = get_encode();
   if (!encode) return xm_set_error(XM_ERR_CUDA, "qgemm: cuTensorMapEncodeTiled unavailable");
-  const int64_t row_bytes = (k / 256) * kRecBytes;
-  const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)n};
+  const int64_t row_bytes = pair_row_bytes<T>(k);
+  const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 2), (cuuint64_t)n};
   const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
-  const cuuint32_t box[2] = {(cuuint32_t)kRecBytes, (cuuint32_t)rows_per_box};
+  const cuuint32_t box[2] = {(cuuint32_t)(ColGeom<T>::BB / 2), (cuuint32_t)rows_per_box};
   const cuuint32_t es[2] = {1, 1};
-  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(w), dims, strides, box, es,
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint8_t*>(w), dims, strides, box, es,
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return xm_set_error(XM_ERR_CUDA, "qgemm: weight tensor map (%d)", (int)r);
   return XM_OK;
 }
 
-template <int NMAP>
+template <int T, int NMAP>
 int launch_pair(const CUtensorMap& map_a, const PairW<NMAP>& pw, int64_t m, int64_t n, int64_t k, int tm,
-                const PairCfg& cfg, int pairs, const float* rowscale, const float* bias, float* y, cudaStream_t st) {
-  const void* fn = pair_kernel<NMAP>();
+                const PairCfg& cfg, int pairs, const float* rowscale, const float* bias, float* y, int acc,
+                cudaStream_t st) {
+  const void* fn = pair_kernel<T, NMAP>();
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, cfg.smem);
   if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemm: smem attribute: %s", cudaGetErrorString(e));
   cudaLaunchConfig_t lc = {};
@@ -988,45 +1114,51 @@ int launch_pair(const CUtensorMap& map_a, const PairW<NMAP>& pw, int64_t m, int6
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = attr;
   lc.numAttrs = 2;
-  e = cudaLaunchKernelEx(&lc, k_qgemm_q4k_pair<kPairDW, NMAP>, map_a, pw, (int)m, (int)n, (int)k, cfg.BN, cfg.NH,
-                         cfg.S, cfg.RW, tm, rowscale, bias, y);
+  e = cudaLaunchKernelEx(&lc, k_qgemm_pair<T, kPairDW, NMAP>, map_a, pw, (int)m, (int)n, (int)k, cfg.BN, cfg.NH,
+                         cfg.S, cfg.RW, tm, rowscale, bias, y, acc);
   if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemm pair launch: %s", cudaGetErrorString(e));
   return xm_check_launch("qgemm pair");
 }
 
 // Dense GEMM on the CTA-pair kernel.  Returns 1 (nothing launched) when the
 // device cannot hold a pair, so the caller can use the single-CTA kernel.
+template <int T>
 int launch_pair_gemm(const CUtensorMap& map_a, const uint8_t* w, int64_t m, int64_t n, int64_t k,
-                     const float* rowscale, const float* bias, float* y, cudaStream_t st) {
-  const int cap = pair_capacity(pair_stages(256, 1));
+                     const float* rowscale, const float* bias, float* y, int acc, cudaStream_t st) {
+  constexpr int BB = ColGeom<T>::BB;
+  const void* fn = pair_kernel<T, 1>();
+  const int cap = pair_capacity(fn, pair_stages(256, 1, BB));
   if (cap < 1) return 1;
   const int64_t mtiles = (m + 255) / 256;
-  const PairCfg cfg = choose_pair(mtiles, n, k, cap);
+  const PairCfg cfg = choose_pair(mtiles, n, k, cap, BB);
   if (cfg.S < 3) return 1;
-  const int cap_cfg = pair_capacity(cfg);
+  const int cap_cfg = pair_capacity(fn, cfg);
   if (cap_cfg < 1) return 1;
   PairW<1> pw{};
-  int rc = encode_w_records(&pw.map[0], w, n, k, cfg.BN / 2);
+  int rc = encode_w_records<T>(&pw.map[0], w, n, k, cfg.BN / 2);
   if (rc) return rc;
   pw.groups = 1;
   const int64_t tiles = mtiles * ((n + cfg.NH * cfg.BN - 1) / (cfg.NH * cfg.BN));
   const int pairs = (int)std::min<int64_t>(tiles, cap_cfg);
-  return launch_pair<1>(map_a, pw, m, n, k, (int)mtiles, cfg, pairs, rowscale, bias, y, st);
+  return launch_pair<T, 1>(map_a, pw, m, n, k, (int)mtiles, cfg, pairs, rowscale, bias, y, acc, st);
 }
 
 // Grouped GEMM (MoE experts) on the CTA-pair kernel; 1 if not possible.
+template <int T>
 int launch_pair_grouped(const CUtensorMap& map_a, const uint8_t* const* h_w, const int* d_cnt, const int* d_off, int G,
                         int64_t P, int64_t n, int64_t k, int64_t max_rows, int64_t expect_rows,
                         const float* rowscale, float* y, cudaStream_t st) {
-  const int cap = pair_capacity(pair_stages(256, 1));
+  constexpr int BB = ColGeom<T>::BB;
+  const void* fn = pair_kernel<T, kMaxGroups>();
+  const int cap = pair_capacity(fn, pair_stages(256, 1, BB));
   if (cap < 1) return 1;
-  const PairCfg cfg = choose_pair((int64_t)G * ((expect_rows + 255) / 256), n, k, cap);
+  const PairCfg cfg = choose_pair((int64_t)G * ((expect_rows + 255) / 256), n, k, cap, BB);
   if (cfg.S < 3) return 1;
-  const int cap_cfg = pair_capacity(cfg);
+  const int cap_cfg = pair_capacity(fn, cfg);
   if (cap_cfg < 1) return 1;
   PairW<kMaxGroups> pw{};
   for (int g = 0; g < G; ++g) {
-    int rc = encode_w_records(&pw.map[g], h_w[g], n, k, cfg.BN / 2);
+    int rc = encode_w_records<T>(&pw.map[g], h_w[g], n, k, cfg.BN / 2);
     if (rc) return rc;
   }
   pw.cnt = d_cnt;
@@ -1035,30 +1167,90 @@ int launch_pair_grouped(const CUtensorMap& map_a, const uint8_t* const* h_w, con
   const int tm = (int)((max_rows + 255) / 256);
   const int64_t tiles = (int64_t)G * tm * ((n + cfg.NH * cfg.BN - 1) / (cfg.NH * cfg.BN));
   const int pairs = (int)std::min<int64_t>(tiles, cap_cfg);
-  return launch_pair<kMaxGroups>(map_a, pw, P, n, k, tm, cfg, pairs, rowscale, nullptr, y, st);
+  return launch_pair<T, kMaxGroups>(map_a, pw, P, n, k, tm, cfg, pairs, rowscale, nullptr, y, 0, st);
 }
+
+// Runtime type id -> the launchers above (dispatch_quant calls operator()<T>).
+struct PairDense {
+  const CUtensorMap* map_a;
+  const uint8_t* w;
+  int64_t m, n, k;
+  const float *rowscale, *bias;
+  float* y;
+  int acc;
+  cudaStream_t st;
+  int rc = 1;
+  template <int T>
+  void operator()() {
+    rc = launch_pair_gemm<T>(*map_a, w, m, n, k, rowscale, bias, y, acc, st);
+  }
+};
+
+struct PairGrouped {
+  const CUtensorMap* map_a;
+  const uint8_t* const* h_w;
+  const int *cnt, *off;
+  int G;
+  int64_t P, n, k, max_rows, expect_rows;
+  const float* rowscale;
+  float* y;
+  cudaStream_t st;
+  int rc = 1;
+  template <int T>
+  void operator()() {
+    rc = launch_pair_grouped<T>(*map_a, h_w, cnt, off, G, P, n, k, max_rows, expect_rows, rowscale, y, st);
+  }
+};
+
+struct RowBytes {
+  int64_t k;
+  int64_t bytes = 0;
+  template <int T>
+  void operator()() {
+    bytes = pair_row_bytes<T>(k);
+  }
+};
 }  // namespace
 
-int qgemm_q4k_grouped(const __half* a16, const float* rowscale, int64_t P, int64_t K, int64_t N,
-                      const uint8_t* const* h_w, const int* d_cnt, const int* d_off, int G, int64_t max_rows,
-                      int64_t expect_rows, float* y, cudaStream_t st) {
+// Bytes of one row of k weights of a block type, or 0 for a type that is not
+// block-quantized.
+int64_t qgemm_row_bytes(int qtype, int64_t k) {
+  RowBytes rb{k};
+  return dispatch_quant(qtype, rb) ? rb.bytes : 0;
+}
+
+bool qgemm_type_supported(int qtype, int64_t k) {
+  if (k < 256 || k % 256) return false;
+  const int64_t rb = qgemm_row_bytes(qtype, k);
+  return rb > 0 && rb % 16 == 0;
+}
+
+int qgemm_grouped(int qtype, const __half* a16, const float* rowscale, int64_t P, int64_t K, int64_t N,
+                  const uint8_t* const* h_w, const int* d_cnt, const int* d_off, int G, int64_t max_rows,
+                  int64_t expect_rows, float* y, cudaStream_t st) {
   if (K % 256 || K < 256 || N < 1 || P < 1 || G < 1 || G > kMaxGroups)
     return xm_set_error(XM_ERR_INVALID, "grouped qgemm: bad shape");
+  if (!qgemm_type_supported(qtype, K))
+    return xm_set_error(XM_ERR_UNSUPPORTED, "grouped qgemm: type id %d rows of k=%lld are not 16-byte multiples", qtype,
+                        (long long)K);
+  CUtensorMap map_a;
+  int rc = encode_a16(&map_a, a16, P, K);
+  if (rc) return rc;
+  PairGrouped pg{&map_a, h_w, d_cnt, d_off, G, P, N, K, max_rows, expect_rows, rowscale, y, st};
+  dispatch_quant(qtype, pg);
+  if (pg.rc != 1) return pg.rc;
+  if (qtype != T_Q4_K)
+    return xm_set_error(XM_ERR_UNSUPPORTED, "grouped qgemm: this device cannot hold the CTA-pair kernel");
   GemmGroups groups{};
   groups.n = G;
   groups.cnt = d_cnt;
   groups.off = d_off;
   for (int g = 0; g < G; ++g) groups.w[g] = h_w[g];
-  CUtensorMap map_a;
-  int rc = encode_a16(&map_a, a16, P, K);
-  if (rc) return rc;
-  rc = launch_pair_grouped(map_a, h_w, d_cnt, d_off, G, P, N, K, max_rows, expect_rows, rowscale, y, st);
-  if (rc != 1) return rc;
   // tile shape for the expected rows per group, grid for the worst case
   TileCfg cfg = choose_tile(expect_rows, N * G, K, sm_count_dev());
   const dim3 grid((unsigned)((N + cfg.BN - 1) / cfg.BN), (unsigned)((max_rows + cfg.MT * 128 - 1) / (cfg.MT * 128)),
                   (unsigned)G);
-  return launch_gemm(map_a, nullptr, P, N, K, cfg, grid, rowscale, nullptr, y, groups, st);
+  return launch_gemm(map_a, nullptr, P, N, K, cfg, grid, rowscale, nullptr, y, 0, groups, st);
 }
 
 extern "C" int64_t xm_qgemm_workspace_size(int64_t m, int64_t k) {
@@ -1066,20 +1258,47 @@ extern "C" int64_t xm_qgemm_workspace_size(int64_t m, int64_t k) {
   return ((m * k * 2 + 255) / 256) * 256 + m * 4;
 }
 
-extern "C" int xm_qgemm(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k, const void* d_x,
-                        int x_dtype, int64_t m, const float* d_bias, float* d_y, void* d_workspace,
-                        int64_t workspace_bytes, void* stream) {
-  if (qtype != T_Q4_K)
-    return xm_set_error(XM_ERR_UNSUPPORTED, "qgemm: type id %d has no tensor-core path yet", qtype);
+namespace {
+template <typename XT>
+void launch_prep(const void* x, int prologue, int64_t m, int64_t k, int64_t ldx, const float* norm_w, float eps,
+                 __half* x16, float* rowscale, cudaStream_t st) {
+  const unsigned pgrid = (unsigned)((m * 32 + 255) / 256);
+  const XT* xt = (const XT*)x;
+  if (prologue == XM_PRO_RMSNORM)
+    k_prep_rows<XT, XM_PRO_RMSNORM><<<pgrid, 256, 0, st>>>(xt, (int)m, (int)k, ldx, norm_w, eps, x16, rowscale);
+  else if (prologue == XM_PRO_SWIGLU)
+    k_prep_rows<XT, XM_PRO_SWIGLU><<<pgrid, 256, 0, st>>>(xt, (int)m, (int)k, ldx, norm_w, eps, x16, rowscale);
+  else
+    k_prep_rows<XT, XM_PRO_NONE><<<pgrid, 256, 0, st>>>(xt, (int)m, (int)k, ldx, norm_w, eps, x16, rowscale);
+}
+}  // namespace
+
+extern "C" int xm_qgemm_ex(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k, const void* d_x,
+                           int x_dtype, int64_t m, int64_t x_stride, int prologue, const float* d_norm_w, float eps,
+                           const float* d_bias, float* d_y, int accumulate, void* d_workspace,
+                           int64_t workspace_bytes, void* stream) {
+  int qk = 0, rec = 0;
+  if (!host_qtype_geometry(qtype, &qk, &rec) || qk == 1)
+    return xm_set_error(XM_ERR_UNSUPPORTED, "qgemm: type id %d is not a block-quantized type", qtype);
   if (m < 1 || n < 1 || k < 256 || k % 256)
     return xm_set_error(XM_ERR_INVALID, "qgemm: need m, n >= 1 and k a positive multiple of 256");
   if (m > (1 << 30) || n > (1 << 30) || k > (1 << 24)) return xm_set_error(XM_ERR_INVALID, "qgemm: shape too large");
   if (x_dtype != XM_DT_F32 && x_dtype != XM_DT_BF16 && x_dtype != XM_DT_F16)
     return xm_set_error(XM_ERR_INVALID, "qgemm: bad x dtype %d", x_dtype);
-  const int64_t row_bytes = (k / 256) * 144;
+  if (prologue != XM_PRO_NONE && prologue != XM_PRO_RMSNORM && prologue != XM_PRO_SWIGLU)
+    return xm_set_error(XM_ERR_INVALID, "qgemm: unknown prologue %d", prologue);
+  if (prologue == XM_PRO_RMSNORM && !d_norm_w) return xm_set_error(XM_ERR_INVALID, "qgemm: RMSNorm needs weights");
+  if (x_stride < (prologue == XM_PRO_SWIGLU ? 2 * k : k))
+    return xm_set_error(XM_ERR_INVALID, "qgemm: x_stride %lld too small", (long long)x_stride);
+  const int64_t row_bytes = qgemm_row_bytes(qtype, k);
   if (n * row_bytes > w_bytes)
     return xm_set_error(XM_ERR_INVALID, "qgemm: weight needs %lld bytes, got %lld", (long long)(n * row_bytes),
                         (long long)w_bytes);
+  if (row_bytes % 16)
+    return xm_set_error(XM_ERR_UNSUPPORTED,
+                        "qgemm: a row of type id %d with k=%lld is %lld bytes, not a multiple of 16 (tensor-map "
+                        "pitch); use the GEMV on row groups",
+                        qtype, (long long)k, (long long)row_bytes);
   if (!d_w || !d_x || !d_y || !d_workspace) return xm_set_error(XM_ERR_INVALID, "qgemm: null pointer");
   if (((uintptr_t)d_w & 15) || ((uintptr_t)d_workspace & 255) || ((uintptr_t)d_x & 15))
     return xm_set_error(XM_ERR_INVALID, "qgemm: weight/x must be 16-byte and workspace 256-byte aligned");
@@ -1089,23 +1308,51 @@ extern "C" int xm_qgemm(int qtype, const void* d_w, int64_t w_bytes, int64_t n, 
 
   __half* x16 = (__half*)d_workspace;
   float* rowscale = (float*)((uint8_t*)d_workspace + ((m * k * 2 + 255) / 256) * 256);
-  const unsigned pgrid = (unsigned)((m * 32 + 255) / 256);
   if (x_dtype == XM_DT_F32)
-    k_prep_rows<float><<<pgrid, 256, 0, st>>>((const float*)d_x, (int)m, (int)k, x16, rowscale);
+    launch_prep<float>(d_x, prologue, m, k, x_stride, d_norm_w, eps, x16, rowscale, st);
   else if (x_dtype == XM_DT_BF16)
-    k_prep_rows<__nv_bfloat16><<<pgrid, 256, 0, st>>>((const __nv_bfloat16*)d_x, (int)m, (int)k, x16, rowscale);
+    launch_prep<__nv_bfloat16>(d_x, prologue, m, k, x_stride, d_norm_w, eps, x16, rowscale, st);
   else
-    k_prep_rows<__half><<<pgrid, 256, 0, st>>>((const __half*)d_x, (int)m, (int)k, x16, rowscale);
+    launch_prep<__half>(d_x, prologue, m, k, x_stride, d_norm_w, eps, x16, rowscale, st);
   int rc = xm_check_launch("qgemm prep");
   if (rc) return rc;
 
   CUtensorMap map_a;
   rc = encode_a16(&map_a, x16, m, k);
   if (rc) return rc;
-  rc = launch_pair_gemm(map_a, (const uint8_t*)d_w, m, n, k, rowscale, d_bias, d_y, st);
-  if (rc != 1) return rc;
+  PairDense pd{&map_a, (const uint8_t*)d_w, m, n, k, rowscale, d_bias, d_y, accumulate ? 1 : 0, st};
+  dispatch_quant(qtype, pd);
+  if (pd.rc != 1) return pd.rc;
+  if (qtype != T_Q4_K)
+    return xm_set_error(XM_ERR_UNSUPPORTED, "qgemm: this device cannot hold the CTA-pair kernel");
   const TileCfg cfg = choose_tile(m, n, k, sm_count_dev());
   const dim3 grid((unsigned)((n + cfg.BN - 1) / cfg.BN), (unsigned)((m + cfg.MT * 128 - 1) / (cfg.MT * 128)));
-  return launch_gemm(map_a, (const uint8_t*)d_w, m, n, k, cfg, grid, rowscale, d_bias, d_y,
+  return launch_gemm(map_a, (const uint8_t*)d_w, m, n, k, cfg, grid, rowscale, d_bias, d_y, accumulate ? 1 : 0,
                      GemmGroups{}, st);
+}
+
+extern "C" int xm_qgemm(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k, const void* d_x,
+                        int x_dtype, int64_t m, const float* d_bias, float* d_y, void* d_workspace,
+                        int64_t workspace_bytes, void* stream) {
+  return xm_qgemm_ex(qtype, d_w, w_bytes, n, k, d_x, x_dtype, m, k, XM_PRO_NONE, nullptr, 0.f, d_bias, d_y, 0,
+                     d_workspace, workspace_bytes, stream);
+}
+
+extern "C" int xm_rmsnorm(const void* d_x, int x_dtype, int64_t m, int64_t k, int64_t x_stride, const float* d_norm_w,
+                          float eps, float* d_out, void* stream) {
+  if (m < 0 || k < 1 || x_stride < k) return xm_set_error(XM_ERR_INVALID, "rmsnorm: bad sizes");
+  if (x_dtype != XM_DT_F32 && x_dtype != XM_DT_BF16 && x_dtype != XM_DT_F16)
+    return xm_set_error(XM_ERR_INVALID, "rmsnorm: bad x dtype %d", x_dtype);
+  if (m == 0) return XM_OK;
+  if (!d_x || !d_norm_w || !d_out) return xm_set_error(XM_ERR_INVALID, "rmsnorm: null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  const unsigned grid = (unsigned)((m * 32 + 255) / 256);
+  if (x_dtype == XM_DT_F32)
+    k_rmsnorm_rows<float><<<grid, 256, 0, st>>>((const float*)d_x, (int)m, (int)k, x_stride, d_norm_w, eps, d_out);
+  else if (x_dtype == XM_DT_BF16)
+    k_rmsnorm_rows<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)d_x, (int)m, (int)k, x_stride,
+                                                         d_norm_w, eps, d_out);
+  else
+    k_rmsnorm_rows<__half><<<grid, 256, 0, st>>>((const __half*)d_x, (int)m, (int)k, x_stride, d_norm_w, eps, d_out);
+  return xm_check_launch("rmsnorm");
 }

@@ -1058,10 +1058,19 @@ extern "C" int xm_qgemv_ex(int qtype, const void* d_w, int64_t w_bytes, int64_t 
                       "16-byte aligned weights and a workspace)");
 }
 
-// Exact-path-only entry (used to cross-check the integer path on the same inputs).
+// Exact-path-only entry (used to cross-check the integer path on the same
+// inputs): always the fp16-exact kernel, whatever the type and shape.
 extern "C" int xm_qgemv_exact(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k, const void* d_x,
                               int x_dtype, int64_t m, const float* d_bias, float* d_y, void* stream) {
-  return xm_qgemv(qtype, d_w, w_bytes, n, k, d_x, x_dtype, m, d_bias, d_y, nullptr, 0, stream);
+  int64_t nb = 0;
+  int rc = check_gemv_args("qgemv_exact", qtype, d_w, w_bytes, n, k, m, &nb);
+  if (rc) return rc;
+  if (x_dtype != XM_DT_F32 && x_dtype != XM_DT_BF16 && x_dtype != XM_DT_F16)
+    return xm_set_error(XM_ERR_INVALID, "qgemv_exact: bad x dtype %d", x_dtype);
+  if (n == 0) return XM_OK;
+  if (!d_x || !d_y) return xm_set_error(XM_ERR_INVALID, "qgemv_exact: null pointer");
+  if (!aligned16(d_x)) return xm_set_error(XM_ERR_INVALID, "qgemv_exact: x not 16-byte aligned");
+  return exact_path(qtype, (const uint8_t*)d_w, n, k, d_x, x_dtype, m, d_bias, d_y, (cudaStream_t)stream);
 }
 
 // ---------------------------------------------------------------------------

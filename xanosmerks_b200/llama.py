@@ -29,7 +29,7 @@ import torch
 
 from . import qtypes
 from ._lib import DT_F32, PRO_NONE, PRO_RMSNORM, PRO_SWIGLU, check, lib
-from .ops import GGUFTensor
+from .ops import GGUFTensor, gemm_supported
 from .synth import make_weight_device
 
 __all__ = ["LlamaConfig", "LlamaWeights", "LlamaDecoder", "synth_llama_weights", "shard_rows", "shard_cols"]
@@ -223,6 +223,7 @@ class LlamaDecoder:
         self.graph = None
         self.length = 0
         self.comm = None
+        self._gemm_ws = None
         if collective not in ("p2p", "nccl"):
             raise ValueError(f"collective must be 'p2p' or 'nccl', got {collective!r}")
         self.collective = collective
@@ -357,13 +358,98 @@ class LlamaDecoder:
         return self.logits
 
     def prefill(self, ids) -> torch.Tensor:
-        """Prompt ids [B, S] -> next token per sequence (the prompt enters the cache)."""
+        """Prompt ids [B, S] -> next token per sequence (the prompt enters the cache).
+
+        A prompt of more than 8 tokens entering an empty cache runs every projection once over all
+        B*S rows on the tensor-core GEMM (RMSNorm, SwiGLU and the residual adds fused as in decode)
+        and the attention in chunks of up to 64 tokens per sequence; shorter prompts, and prompts
+        appended to a filled cache, go 8 tokens at a time through the decode path."""
         ids = torch.as_tensor(np.asarray(ids) if not isinstance(ids, torch.Tensor) else ids)
-        S = ids.shape[1]
+        B, S = ids.shape
+        if S > self.LQ_MAX and self.length == 0:
+            return self._prefill_gemm(ids)
         out = None
         for s0 in range(0, S, self.LQ_MAX):
             out = self.forward_tokens(ids[:, s0:s0 + self.LQ_MAX])
         return out
+
+    PREFILL_CHUNK = 64
+
+    def _gemm(self, wt: GGUFTensor, x: torch.Tensor, rows: int, y: torch.Tensor, prologue=PRO_NONE, norm=None,
+              accumulate=False):
+        """y[:rows] (+)= pro(x[:rows]) @ W.T on the tensor-core GEMM (GEMV groups where the type's row
+        pitch does not suit the GEMM)."""
+        n, k = wt.shape
+        if not gemm_supported(wt.qtype, k):
+            self._gemv(wt, x, rows, y, prologue, norm, accumulate)
+            return
+        need = lib.xm_qgemm_workspace_size(rows, k)
+        if self._gemm_ws is None or self._gemm_ws.numel() < need:
+            self._gemm_ws = torch.empty(need, dtype=torch.uint8, device=self.dev)
+        check(lib.xm_qgemm_ex(wt.qtype.type_id, wt.data.data_ptr(), wt.nbytes, n, k, x.data_ptr(), DT_F32, rows,
+                              x.stride(0), prologue, norm.data_ptr() if norm is not None else None,
+                              self.cfg.norm_eps, None, y.data_ptr(), 1 if accumulate else 0,
+                              self._gemm_ws.data_ptr(), self._gemm_ws.numel(), self._stream()), "qgemm_ex")
+
+    def _prefill_gemm(self, ids: torch.Tensor) -> torch.Tensor:
+        cfg, B = self.cfg, self.B
+        S = ids.shape[1]
+        if ids.shape[0] != B:
+            raise ValueError(f"ids must be [{B}, S], got {tuple(ids.shape)}")
+        if S > self.max_ctx:
+            raise ValueError(f"context overflow: {S} > {self.max_ctx}")
+        lo, hi = int(ids.min()), int(ids.max())
+        if lo < 0 or hi >= cfg.vocab_size:
+            raise ValueError(f"token ids must lie in [0, {cfg.vocab_size}), got [{lo}, {hi}]")
+        rows = B * S                                       # row b*S + s: token s of sequence b
+        D, hd = cfg.hidden_size, cfg.head_dim
+        f32 = dict(dtype=torch.float32, device=self.dev)
+        h = torch.empty(rows, D, **f32)
+        qkv = torch.empty(rows, self.qkv_dim, **f32)
+        attn = torch.empty(rows, self.hq * hd, **f32)
+        gu = torch.empty(rows, 2 * self.f_l, **f32)
+        part = torch.empty(rows, D, **f32) if self.world > 1 else None
+        idv = ids.reshape(-1).to(self.dev, torch.int32).contiguous()
+        chunk_pos = torch.arange(0, S, self.PREFILL_CHUNK, dtype=torch.int32, device=self.dev)
+        st = self._stream()
+        e = self.w.embed
+        check(lib.xm_embed(e.qtype.type_id, e.data.data_ptr(), e.nbytes, e.shape[0], e.shape[1], idv.data_ptr(),
+                           rows, h.data_ptr(), st), "embed")
+        for li, lw in enumerate(self.w.layers):
+            self._gemm(lw["qkv"], h, rows, qkv, PRO_RMSNORM, lw["attn_norm"])
+            for b in range(B):
+                for ci, c0 in enumerate(range(0, S, self.PREFILL_CHUNK)):
+                    lq = min(self.PREFILL_CHUNK, S - c0)
+                    r0 = b * S + c0
+                    check(lib.xm_attention(qkv[r0].data_ptr(), self.qkv_dim, self.kc[li, b].data_ptr(),
+                                           self.vc[li, b].data_ptr(), chunk_pos[ci].data_ptr(), 1, lq, self.hq,
+                                           self.hk, hd, cfg.rope_theta, self.max_ctx, attn[r0].data_ptr(),
+                                           self.hq * hd, self.attn_ws.data_ptr(), self.attn_ws.numel(), st),
+                          "attention")
+            if self.world == 1:
+                self._gemm(lw["o"], attn, rows, h, accumulate=True)
+            else:
+                self._gemm(lw["o"], attn, rows, part)
+                self._allreduce_rows(h, part)
+            self._gemm(lw["gate_up"], h, rows, gu, PRO_RMSNORM, lw["ffn_norm"])
+            if self.world == 1:
+                self._gemm(lw["down"], gu, rows, h, PRO_SWIGLU, accumulate=True)
+            else:
+                self._gemm(lw["down"], gu, rows, part, PRO_SWIGLU)
+                self._allreduce_rows(h, part)
+        # the output head on each sequence's last token (the decode state keeps those rows)
+        last = h.view(B, S, D)[:, S - 1]
+        self.h[:B].copy_(last)
+        self._head(1)
+        self.pos0.fill_(S)
+        self.length = S
+        return self.next_ids
+
+    def _allreduce_rows(self, h, part):
+        """h += sum over ranks of part (the prefill's row-parallel outputs, NCCL all-reduce)."""
+        import torch.distributed as dist
+        dist.all_reduce(part, group=self.pg)
+        h.add_(part)
 
     def decode_step(self):
         """One greedy step from device state: the token in next_ids enters at pos0."""

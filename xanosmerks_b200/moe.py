@@ -8,7 +8,8 @@ expert weights given as :class:`~xanosmerks_b200.ops.GGUFTensor` (blocks
 resident on the GPU).  The same argument checks and exceptions as the
 reference are raised.  The forward pass runs entirely on the GPU
 (``xm_moe_forward``): routing, stable sort by expert, grouped tensor-core
-GEMMs, SwiGLU and the ordered combine.
+GEMMs, the gated activation (``hidden_act``: silu/swish, gelu, relu or
+identity, as the reference's ``apply_activation``) and the ordered combine.
 """
 
 from __future__ import annotations
@@ -18,14 +19,15 @@ import ctypes
 import numpy as np
 import torch
 
-from ._lib import DT_BF16, DT_F16, DT_F32, check, lib
-from .ops import GGUFTensor, _back, _to_device_x, _workspace
+from ._lib import ACT, DT_BF16, DT_F16, DT_F32, XMError, check, lib
+from .ops import GGUFTensor, _workspace
 
 _DT = {torch.float32: DT_F32, torch.bfloat16: DT_BF16, torch.float16: DT_F16}
 
 
 class MoELayer:
-    """Sparse (top-k) or dense (k == E) mixture of SwiGLU experts."""
+    """Sparse (top-k) or dense (k == E) mixture of gated experts, act(x W1.T) * (x W3.T) then W2
+    (act: the reference's ``hidden_act``, silu by default)."""
 
     def __init__(self, config, weights):
         self.num_experts = config["num_experts"]
@@ -36,8 +38,9 @@ class MoELayer:
         if self.num_experts_per_tok > self.num_experts:
             raise ValueError(f"MoELayer: num_experts_per_tok={self.num_experts_per_tok} "
                              f"> num_experts={self.num_experts}")
-        if self.activation not in ("silu", "swish"):
-            raise NotImplementedError(f"MoELayer on the GPU supports silu experts, not {self.activation}")
+        if self.activation not in ACT:
+            raise ValueError(f"MoELayer: unknown activation {self.activation!r} (apply_activation knows "
+                             f"{sorted(ACT)})")
         gate_w = weights["gate"]["weight"]
         gate_w = gate_w if isinstance(gate_w, torch.Tensor) else torch.as_tensor(np.asarray(gate_w, np.float32))
         if gate_w.ndim != 2:
@@ -75,17 +78,28 @@ class MoELayer:
         T = xf.shape[0]
         out = torch.empty((T, H), dtype=torch.float32, device=x.device)
         wsz = lib.xm_moe_workspace_size(T, H, F, E, k)
-        ws = _workspace(x.device, wsz)
         with torch.cuda.device(x.device):
+            stream = torch.cuda.current_stream(x.device)
+            ws = _workspace(x.device, stream, wsz)
             check(lib.xm_moe_forward(xf.data_ptr(), _DT[xf.dtype], T, H, self.gate.data_ptr(), E, k, F,
-                                     self._p1, self._p3, self._p2, self.qtype, out.data_ptr(), ws.data_ptr(),
-                                     ws.numel(), torch.cuda.current_stream(x.device).cuda_stream), "moe")
+                                     self._p1, self._p3, self._p2, self.qtype, ACT[self.activation], out.data_ptr(),
+                                     ws.data_ptr(), ws.numel(), stream.cuda_stream), "moe")
         return out.reshape(x.shape)
 
     def __call__(self, x):
-        """x: (batch, seq, hidden) -> (batch, seq, hidden), as moe.py:54-115."""
-        xd, how = _to_device_x(x, self.device)
-        return _back(self.forward_device(xd), how)
+        """x: (batch, seq, hidden) -> (batch, seq, hidden), as moe.py:54-115.  A numpy x gives a
+        numpy fp32 result (the device error word is checked once the result is on the host)."""
+        if isinstance(x, torch.Tensor) and x.is_cuda:
+            return self.forward_device(x)
+        numpy_in = not isinstance(x, torch.Tensor)
+        xt = torch.from_numpy(np.ascontiguousarray(np.asarray(x, dtype=np.float32))) if numpy_in else x
+        y = self.forward_device(xt.to(self.device))
+        with torch.cuda.device(self.device):
+            res = y.cpu()
+            st = lib.xm_device_status(1)
+        if st:
+            raise XMError(f"MoELayer: a bounded wait inside a kernel gave up (device error word {st})")
+        return res.numpy() if numpy_in else res
 
     def __repr__(self):
         mode = "dense" if self._is_dense else f"top-{self.num_experts_per_tok}"
@@ -113,8 +127,9 @@ class MoELayerEP:
             raise ValueError(f"MoELayerEP: num_experts_per_tok={k} outside 1..{E}")
         if E % world:
             raise ValueError(f"MoELayerEP: {E} experts do not divide over {world} ranks")
-        if config.get("hidden_act", "silu") not in ("silu", "swish"):
-            raise NotImplementedError("MoELayerEP supports silu experts")
+        self.activation = config.get("hidden_act", "silu")
+        if self.activation not in ACT:
+            raise ValueError(f"MoELayerEP: unknown activation {self.activation!r}")
         self.rank, self.world = rank, world
         self.pg = process_group if process_group is not None else dist.group.WORLD
         self.e_local = E // world
@@ -150,8 +165,9 @@ class MoELayerEP:
         xf = x.reshape(-1, H).contiguous()
         T = xf.shape[0]
         dev = x.device
-        st = torch.cuda.current_stream(dev).cuda_stream
-        ws = _workspace(dev, lib.xm_moe_workspace_size(T, H, F, E, k))
+        stream = torch.cuda.current_stream(dev)
+        st = stream.cuda_stream
+        ws = _workspace(dev, stream, lib.xm_moe_workspace_size(T, H, F, E, k))
         send = torch.empty((T * k, H), dtype=xf.dtype, device=dev)
         cnt = torch.empty(E, dtype=torch.int32, device=dev)
         with torch.cuda.device(dev):
@@ -169,7 +185,8 @@ class MoELayerEP:
                     keep.extend((g_cnt, g_off, ews))
                     check(lib.xm_moe_experts(recv.data_ptr(), _DT[xf.dtype], R, H, F, W * El, g_cnt.data_ptr(),
                                              g_off.data_ptr(), self._p1, self._p3, self._p2, self.qtype,
-                                             int(rc.max()), rows.data_ptr(), ews.data_ptr(), ews.numel(), st),
+                                             ACT[self.activation], int(rc.max()), rows.data_ptr(), ews.data_ptr(),
+                                             ews.numel(), st),
                           "moe_experts")
                 return rows
 
