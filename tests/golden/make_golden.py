@@ -2,7 +2,7 @@
 
 Run (in a checkout that has the reference's sources available):
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <path to the reference package sources>
 
 It builds a throwaway package of symlinks to the reference's hot-path modules
 (gguf_dequant.py, dtype_ops.py, ops.py, primitives.py, moe.py) so their relative
@@ -174,7 +174,8 @@ def moe_cases(ref):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("XM_REFERENCE_DIR"), required="XM_REFERENCE_DIR" not in os.environ,
+                    help="directory holding the reference modules (or set XM_REFERENCE_DIR)")
     args = ap.parse_args()
     ref = load_reference(args.reference)
     np.savez_compressed(os.path.join(HERE, "golden_dequant.npz"), **dequant_cases(ref))

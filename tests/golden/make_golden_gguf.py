@@ -3,7 +3,7 @@ reference's own parser reads them.
 
 Run (in a checkout that has the reference's sources available):
 
-    python tests/golden/make_golden_gguf.py --reference /root/reference
+    python tests/golden/make_golden_gguf.py --reference <path to the reference package sources>
 
 It writes small GGUF files with a writer of its own (every metadata value type,
 nested arrays, default and non-default alignment, GGUF versions 2 and 3,

@@ -28,7 +28,7 @@ import numpy as np
 import torch
 
 from . import qtypes
-from ._lib import DT_F32, PRO_NONE, PRO_RMSNORM, PRO_SWIGLU, check, lib
+from ._lib import DT_F32, PRO_NONE, PRO_RMSNORM, PRO_SWIGLU, check, check_device, lib
 from .ops import GGUFTensor, gemm_supported
 from .synth import make_weight_device
 
@@ -479,12 +479,20 @@ class LlamaDecoder:
             self.graph.replay()
         self.length += n
 
+    def check(self):
+        """Raise if a bounded wait inside any kernel since the last check gave up (a tensor-parallel
+        peer that never arrived, a lost bulk copy); synchronises the device.  ``generate`` calls it
+        after every token; callers that drive ``replay`` themselves call it where they read results."""
+        with torch.cuda.device(self.dev):
+            check_device("LlamaDecoder")
+
     def generate(self, prompt, max_new_tokens: int, use_graph: bool = True) -> np.ndarray:
         """Greedy generation: prompt [B, S] -> generated ids [B, max_new_tokens]."""
         self.reset()
         out = np.zeros((self.B, max_new_tokens), dtype=np.int64)
         nxt = self.prefill(prompt)
         out[:, 0] = nxt.cpu().numpy()
+        self.check()
         for t in range(1, max_new_tokens):
             if use_graph:
                 if self.graph is None:
@@ -498,4 +506,5 @@ class LlamaDecoder:
                 self.decode_step()
                 self.length += 1
             out[:, t] = self.next_ids.cpu().numpy()
+            self.check()
         return out
