@@ -74,6 +74,9 @@ def parse():
                     help="profiling mode: two graph-replayed decode steps of this batch size between "
                          "cudaProfilerStart/Stop (with --decode-layers layers)")
     ap.add_argument("--decode-layers", type=int, default=2)
+    ap.add_argument("--prefill-profile", type=int, default=0,
+                    help="profiling mode: a prefill of this many tokens (batch 1, --decode-layers layers) "
+                         "between cudaProfilerStart/Stop")
     ap.add_argument("--gemm-m", type=int, default=0,
                     help="only time the prefill GEMM with this many activation rows (profiling mode)")
     ap.add_argument("--gemm-type", default="Q4_K", help="block type of --gemm-m / --gemv-only")
@@ -855,6 +858,25 @@ def run_decode_profile(args):
     print(json.dumps({"decode_profile": B, "layers": args.decode_layers, "ok": True}), flush=True)
 
 
+def run_prefill_profile(args):
+    """Profiling mode: the bench's Llama shapes with --decode-layers layers; one warm-up prefill of a
+    --prefill-profile-token prompt (batch 1), then a second one between cudaProfilerStart/Stop."""
+    import torch
+    from xanosmerks_b200.llama import LlamaConfig, LlamaDecoder, LlamaWeights, synth_llama_weights
+    cfg = LlamaConfig(num_layers=args.decode_layers)
+    w = LlamaWeights.from_full(cfg, synth_llama_weights(cfg, seed=0, device="cuda"))
+    dec = LlamaDecoder(w, batch=1, max_ctx=640)
+    ids = torch.from_numpy(np.random.default_rng(0).integers(0, cfg.vocab_size, size=(1, args.prefill_profile)))
+    dec.prefill(ids)
+    dec.reset()
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStart()
+    ms = event_ms(lambda: dec.prefill(ids))
+    torch.cuda.cudart().cudaProfilerStop()
+    print(json.dumps({"prefill_profile": args.prefill_profile, "layers": args.decode_layers, "ms": round(ms, 3)}),
+          flush=True)
+
+
 def moe_case(dev, T=1024, E=8, k=2, H=4096, F=14336, seed=0):
     """Mixtral-shape MoE block with random-init Q4_K experts (seeded)."""
     import torch
@@ -902,6 +924,9 @@ def main():
         return
     if args.decode_profile:
         run_decode_profile(args)
+        return
+    if args.prefill_profile:
+        run_prefill_profile(args)
         return
     if args.gemm_m:
         run_gemm_only(args)

@@ -138,3 +138,85 @@ XM_DEV bool smem_wait_eq(const volatile int* p, int want) {
   atomicOr(&g_xm_device_error, XM_DEVERR_TIMEOUT);
   return false;
 }
+
+// ---------------------------------------------------------------------------
+// Row preparation of tensor-core GEMM activations: one 256-thread block per
+// row, 4 consecutive values per thread per step (vector loads), the row's
+// values converted to fp16 after division by a power of two that puts the
+// row's largest magnitude in [2^14, 2^15) (exact for bf16 and fp16 input;
+// keeps large and tiny rows inside fp16's range).
+// ---------------------------------------------------------------------------
+constexpr int kPrepThreads = 256;
+
+// 4 consecutive values as fp32 (p 8-byte aligned for 16-bit types, 16-byte for fp32)
+template <typename T> XM_DEV void ld4f(const T* p, float (&v)[4]);
+template <> XM_DEV void ld4f<float>(const float* p, float (&v)[4]) {
+  const float4 f = *reinterpret_cast<const float4*>(p);
+  v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+}
+template <> XM_DEV void ld4f<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  v[0] = __uint_as_float(u.x << 16); v[1] = __uint_as_float(u.x & 0xFFFF0000u);
+  v[2] = __uint_as_float(u.y << 16); v[3] = __uint_as_float(u.y & 0xFFFF0000u);
+}
+template <> XM_DEV void ld4f<__half>(const __half* p, float (&v)[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+
+// block-wide max / sum of one value per thread (kPrepThreads threads; red: 32 floats)
+XM_DEV float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = red[0];
+  for (int w = 1; w < kPrepThreads / 32; ++w) r = fmaxf(r, red[w]);
+  __syncthreads();
+  return r;
+}
+XM_DEV float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = red[0];
+  for (int w = 1; w < kPrepThreads / 32; ++w) r += red[w];
+  __syncthreads();
+  return r;
+}
+
+// The power-of-two exponent s with amax / 2^s in [2^14, 2^15) (0 for zero or non-finite rows).
+XM_DEV int fp16_row_shift(float amax) {
+  int s = 0;
+  if (amax > 0.f && amax < INFINITY) {
+    int e;
+    frexpf(amax, &e);           // amax = f * 2^e, f in [0.5, 1): amax in [2^(e-1), 2^e)
+    s = (e - 1) - 14;
+  }
+  return s;
+}
+
+// One row: val(k, v) writes the 4 values at k (k % 4 == 0); out[k] = fp16(v / 2^s),
+// *scale = 2^s.  Every thread of the block calls it; K % 4 == 0.
+template <typename F>
+XM_DEV void prep_row_fp16(F val, int K, __half* __restrict__ out, float* __restrict__ scale, float* red) {
+  float amax = 0.f;
+  for (int k = threadIdx.x * 4; k < K; k += kPrepThreads * 4) {
+    float v[4];
+    val(k, v);
+    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3]))));
+  }
+  amax = block_max(amax, red);
+  const int s = fp16_row_shift(amax);
+  const float inv = ldexpf(1.0f, -s);
+  for (int k = threadIdx.x * 4; k < K; k += kPrepThreads * 4) {
+    float v[4];
+    val(k, v);
+    const __half2 a = __floats2half2_rn(v[0] * inv, v[1] * inv), b = __floats2half2_rn(v[2] * inv, v[3] * inv);
+    *reinterpret_cast<uint2*>(out + k) = make_uint2(*reinterpret_cast<const uint32_t*>(&a),
+                                                    *reinterpret_cast<const uint32_t*>(&b));
+  }
+  if (threadIdx.x == 0) *scale = ldexpf(1.0f, s);
+}

@@ -19,6 +19,7 @@ constexpr int kHeadDim = 128;
 constexpr int kAttnKeys = 64;    // keys per attention CTA
 constexpr int kMaxGroup = 8;     // query heads per KV head
 constexpr int kMaxLq = 64;       // new tokens per sequence in one call (a prefill chunk)
+constexpr int kAttnTokensPerCta = 4;   // new tokens a CTA takes in turn (more tokens: more CTAs)
 
 // ---------------------------------------------------------------------------
 // out[b][:] = fp16-rounded dequantized row ids[b] of a GGUF table (the
@@ -74,7 +75,10 @@ struct EmbedLaunch {
 // written to the cache and used from shared memory.  Each CTA rotates the
 // query rows itself, writes its partial (max, sum, unnormalised output) per
 // (token, head) to the workspace, and the last CTA of (b, hk) to finish merges
-// the partials in split order into out[b*Lq + j][hq][128].
+// the partials in split order into out[b*Lq + j][hq][128].  With many new
+// tokens (a prefill chunk) the tokens are dealt over gridDim.z groups of CTAs
+// (token j to group j % Z), each group with the same key tiles; group 0
+// appends the new keys and values to the cache.
 // ---------------------------------------------------------------------------
 struct AttnPart {
   float m, l;
@@ -105,6 +109,7 @@ __global__ void __launch_bounds__(256) k_attention(const float* __restrict__ qkv
   grid_dep_wait();
   grid_dep_launch();
   const int b = blockIdx.x / Hk, hk = blockIdx.x % Hk, s = blockIdx.y;
+  const int z = blockIdx.z, Z = gridDim.z;       // this CTA's tokens: j = z, z + Z, ...
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = Hq / Hk;
   const int p0 = pos0[b];
@@ -142,16 +147,18 @@ __global__ void __launch_bounds__(256) k_attention(const float* __restrict__ qkv
       const float va = row[(Hk + hk) * kHeadDim + d], vb = row[(Hk + hk) * kHeadDim + d + 64];
       const __half hka = __float2half_rn(ka), hkb = __float2half_rn(kb);
       const __half hva = __float2half_rn(va), hvb = __float2half_rn(vb);
-      K[(int64_t)pos * kHeadDim + d] = hka;
-      K[(int64_t)pos * kHeadDim + d + 64] = hkb;
-      V[(int64_t)pos * kHeadDim + d] = hva;
-      V[(int64_t)pos * kHeadDim + d + 64] = hvb;
+      if (z == 0) {                                  // one token group appends to the cache
+        K[(int64_t)pos * kHeadDim + d] = hka;
+        K[(int64_t)pos * kHeadDim + d + 64] = hkb;
+        V[(int64_t)pos * kHeadDim + d] = hva;
+        V[(int64_t)pos * kHeadDim + d + 64] = hvb;
+      }
       reinterpret_cast<__half*>(&ks[r][0])[d] = hka;
       reinterpret_cast<__half*>(&ks[r][0])[d + 64] = hkb;
       reinterpret_cast<__half*>(&vs[r][0])[d] = hva;
       reinterpret_cast<__half*>(&vs[r][0])[d + 64] = hvb;
     }
-    for (int j = 0; j < Lq; ++j) {
+    for (int j = z; j < Lq; j += Z) {
       const int len = p0 + j + 1;                    // token j sees keys < len
       const int nkj = min(kend, len) - k0;           // keys of this tile it sees (may be <= 0)
       __syncthreads();                               // tiles staged / previous token done with qs, sc
@@ -222,7 +229,7 @@ __global__ void __launch_bounds__(256) k_attention(const float* __restrict__ qkv
   // the last CTA of (b, hk) merges
   __threadfence();
   __syncthreads();
-  if (tid == 0) last = atomicAdd(&tickets[bh], 1) == nsplit - 1;
+  if (tid == 0) last = atomicAdd(&tickets[bh], 1) == nsplit * Z - 1;
   __syncthreads();
   if (!last) return;
   __threadfence();
@@ -360,7 +367,8 @@ int xm_attention(const float* d_qkv, int64_t qkv_stride, void* d_kcache, void* d
   AttnPart* part_ml = (AttnPart*)(part_o + cells * kHeadDim);
   int* tickets = (int*)(part_ml + cells);
   // tickets start at zero (the caller zeroes the workspace once) and every call leaves them at zero
-  return launch_status(launch_pdl(k_attention, dim3((unsigned)(B * Hk), (unsigned)nsplit), dim3(256),
+  const unsigned Z = (unsigned)((Lq + kAttnTokensPerCta - 1) / kAttnTokensPerCta);
+  return launch_status(launch_pdl(k_attention, dim3((unsigned)(B * Hk), (unsigned)nsplit, Z), dim3(256),
                                   (cudaStream_t)stream, d_qkv, qkv_stride, (__half*)d_kcache, (__half*)d_vcache,
                                   d_pos0, Lq, Hq, Hk, (int)max_ctx, nsplit, theta, part_o, part_ml, tickets, d_out,
                                   out_stride),

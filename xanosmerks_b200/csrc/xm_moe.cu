@@ -9,13 +9,14 @@
 //   output[token] += expert_out * weight, experts in ascending order (moe.py:112)
 //
 // Device pipeline (one stream, no host round trip):
-//   k_moe_router      one warp per token: E dot products, top-k, softmax
+//   k_moe_router      one warp per token: E dot products (vector loads), top-k, softmax
 //   k_moe_sort        one CTA: stable counting sort of the T*k pairs by expert
 //   k_moe_gather_prep gathered rows of x -> fp16 with a power-of-two row scale
 //   grouped GEMM      w1 and w3 over every expert's row range (tensor cores)
 //   k_swiglu_prep     silu(g) * u -> fp16 with row scale (A of the next GEMM)
 //   grouped GEMM      w2
 //   k_moe_combine     weighted sum of each token's k expert rows, ascending expert
+//                     (one block per token)
 #include <algorithm>
 
 #include "xm_internal.h"
@@ -38,42 +39,61 @@ XM_DEV void softmax_small(float* v, int n) {
   for (int i = 0; i < n; ++i) v[i] = v[i] / (s + 1e-12f);
 }
 
-template <typename XT>
+// One warp per token.  Lane l covers elements 8l + 256i of the row (vector
+// loads of x and of every expert's gate row); the E <= EC logits stay in
+// registers (static indices only), go through shared memory after the warp
+// reduction, and lane 0 selects the top k from there.
+template <typename XT, int EC>
 __global__ void __launch_bounds__(256) k_moe_router(const XT* __restrict__ x, const float* __restrict__ gate, int T,
                                                     int H, int E, int k, int* __restrict__ topk_e,
                                                     float* __restrict__ topk_w) {
-  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  __shared__ float s_logit[8][EC];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + warp;
   if (t >= T) return;
-  float acc[kMaxExperts];
+  float acc[EC];
 #pragma unroll
-  for (int e = 0; e < kMaxExperts; ++e) acc[e] = 0.f;
+  for (int e = 0; e < EC; ++e) acc[e] = 0.f;
   const XT* xr = x + (int64_t)t * H;
-  for (int h = lane; h < H; h += 32) {
-    const float xv = to_f32(xr[h]);
+  for (int h = lane * 8; h < H; h += 256) {
+    float xv[8];
+    ld4f<XT>(xr + h, *reinterpret_cast<float(*)[4]>(xv));
+    ld4f<XT>(xr + h + 4, *reinterpret_cast<float(*)[4]>(xv + 4));
 #pragma unroll
-    for (int e = 0; e < kMaxExperts; ++e)
-      if (e < E) acc[e] = fmaf(xv, gate[(int64_t)e * H + h], acc[e]);
+    for (int e = 0; e < EC; ++e) {
+      if (e < E) {
+        const float4 g0 = __ldg(reinterpret_cast<const float4*>(gate + (int64_t)e * H + h));
+        const float4 g1 = __ldg(reinterpret_cast<const float4*>(gate + (int64_t)e * H + h + 4));
+        float a = acc[e];
+        a = fmaf(xv[0], g0.x, a); a = fmaf(xv[1], g0.y, a); a = fmaf(xv[2], g0.z, a); a = fmaf(xv[3], g0.w, a);
+        a = fmaf(xv[4], g1.x, a); a = fmaf(xv[5], g1.y, a); a = fmaf(xv[6], g1.z, a); a = fmaf(xv[7], g1.w, a);
+        acc[e] = a;
+      }
+    }
   }
 #pragma unroll
-  for (int e = 0; e < kMaxExperts; ++e) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
+  for (int e = 0; e < EC; ++e) {
+    if (e < E) {
+      const float v = warp_sum(acc[e]);
+      if (lane == 0) s_logit[warp][e] = v;
+    }
   }
+  __syncwarp();
   if (lane != 0) return;
-  int sel[kMaxExperts];
-  float val[kMaxExperts];
+  const float* lg = s_logit[warp];
+  int sel[EC];
+  float val[EC];
   if (k == E) {
-    for (int e = 0; e < E; ++e) { sel[e] = e; val[e] = acc[e]; }
+    for (int e = 0; e < E; ++e) { sel[e] = e; val[e] = lg[e]; }
   } else {
-    bool used[kMaxExperts];
-    for (int e = 0; e < E; ++e) used[e] = false;
+    unsigned used = 0;
     for (int j = 0; j < k; ++j) {       // the k largest logits (the set argpartition selects)
       int best = -1;
       for (int e = 0; e < E; ++e)
-        if (!used[e] && (best < 0 || acc[e] > acc[best])) best = e;
-      used[best] = true;
+        if (!((used >> e) & 1u) && (best < 0 || lg[e] > lg[best])) best = e;
+      used |= 1u << best;
       sel[j] = best;
-      val[j] = acc[best];
+      val[j] = lg[best];
     }
   }
   softmax_small(val, k);
@@ -138,30 +158,17 @@ __global__ void __launch_bounds__(1024) k_moe_sort(const int* __restrict__ topk_
   }
 }
 
-// Rows are converted to fp16 with a power-of-two scale putting the row's max
-// magnitude in [2^14, 2^15) (exact for bf16 input; the same rule as the
-// prefill GEMM's activation preparation).
+// Rows (gathered in expert order) converted to fp16 with a power-of-two row
+// scale (prep_row_fp16: the prefill GEMM's activation preparation).
 template <typename XT>
-__global__ void __launch_bounds__(256) k_moe_gather_prep(const XT* __restrict__ x, const int* __restrict__ sorted_tok,
-                                                         int P, int H, __half* __restrict__ a16,
-                                                         float* __restrict__ ascale) {
-  const int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (p >= P) return;
+__global__ void __launch_bounds__(kPrepThreads) k_moe_gather_prep(const XT* __restrict__ x,
+                                                                  const int* __restrict__ sorted_tok, int P, int H,
+                                                                  __half* __restrict__ a16,
+                                                                  float* __restrict__ ascale) {
+  __shared__ float red[32];
+  const int p = blockIdx.x;
   const XT* xr = x + (int64_t)(sorted_tok ? sorted_tok[p] : p) * H;
-  float amax = 0.f;
-  for (int i = lane; i < H; i += 32) amax = fmaxf(amax, fabsf(to_f32(xr[i])));
-#pragma unroll
-  for (int s = 16; s > 0; s >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, s));
-  int sh = 0;
-  if (amax > 0.f && amax < INFINITY) {
-    int e;
-    frexpf(amax, &e);
-    sh = (e - 1) - 14;
-  }
-  const float inv = ldexpf(1.0f, -sh);
-  __half* o = a16 + (int64_t)p * H;
-  for (int i = lane; i < H; i += 32) o[i] = __float2half_rn(to_f32(xr[i]) * inv);
-  if (lane == 0) ascale[p] = ldexpf(1.0f, sh);
+  prep_row_fp16([&](int k, float (&v)[4]) { ld4f<XT>(xr + k, v); }, H, a16 + (int64_t)p * H, ascale + p, red);
 }
 
 // send[p] = x[sorted_tok[p]] (rows in expert order, x's element type kept)
@@ -187,53 +194,65 @@ XM_DEV float expert_act(float x) {
 }
 
 template <int ACT>
-__global__ void __launch_bounds__(256) k_swiglu_prep(const float* __restrict__ g, const float* __restrict__ u, int P,
-                                                     int F, __half* __restrict__ h16, float* __restrict__ hscale) {
-  const int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (p >= P) return;
+__global__ void __launch_bounds__(kPrepThreads) k_swiglu_prep(const float* __restrict__ g, const float* __restrict__ u,
+                                                              int P, int F, __half* __restrict__ h16,
+                                                              float* __restrict__ hscale) {
+  __shared__ float red[32];
+  const int p = blockIdx.x;
   const float* gr = g + (int64_t)p * F;
   const float* ur = u + (int64_t)p * F;
-  float amax = 0.f;
-  for (int i = lane; i < F; i += 32) amax = fmaxf(amax, fabsf(expert_act<ACT>(gr[i]) * ur[i]));
+  prep_row_fp16(
+      [&](int k, float (&v)[4]) {
+        float uu[4];
+        ld4f<float>(gr + k, v);
+        ld4f<float>(ur + k, uu);
 #pragma unroll
-  for (int s = 16; s > 0; s >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, s));
-  int sh = 0;
-  if (amax > 0.f && amax < INFINITY) {
-    int e;
-    frexpf(amax, &e);
-    sh = (e - 1) - 14;
-  }
-  const float inv = ldexpf(1.0f, -sh);
-  __half* o = h16 + (int64_t)p * F;
-  for (int i = lane; i < F; i += 32) o[i] = __float2half_rn(expert_act<ACT>(gr[i]) * ur[i] * inv);
-  if (lane == 0) hscale[p] = ldexpf(1.0f, sh);
+        for (int i = 0; i < 4; ++i) v[i] = expert_act<ACT>(v[i]) * uu[i];
+      },
+      F, h16 + (int64_t)p * F, hscale + p, red);
 }
 
 // out[t] = sum over the token's k expert rows, ascending expert order, of
-// row * weight: products rounded, then added, as the numpy accumulation does.
+// row * weight: products rounded, then added, as the numpy accumulation does
+// (moe.py:110-113).  One block per token: the token's k (expert, row, weight)
+// triples are ordered once in shared memory, then every thread sums 4
+// consecutive columns (vector loads).
 __global__ void __launch_bounds__(256) k_moe_combine(const float* __restrict__ d, const int* __restrict__ topk_e,
                                                      const float* __restrict__ topk_w, const int* __restrict__ pair_pos,
                                                      int T, int H, int k, float* __restrict__ out) {
-  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (t >= T) return;
-  int ord[kMaxExperts];
-  for (int j = 0; j < k; ++j) ord[j] = j;
-  for (int a = 1; a < k; ++a) {            // insertion sort of the k slots by expert id
-    const int v = ord[a];
-    int b = a - 1;
-    while (b >= 0 && topk_e[(int64_t)t * k + ord[b]] > topk_e[(int64_t)t * k + v]) {
-      ord[b + 1] = ord[b];
-      --b;
+  __shared__ int s_pos[kMaxExperts];
+  __shared__ float s_w[kMaxExperts];
+  const int t = blockIdx.x;
+  if (threadIdx.x == 0) {
+    int ord[kMaxExperts];
+    for (int j = 0; j < k; ++j) ord[j] = j;
+    for (int a = 1; a < k; ++a) {            // insertion sort of the k slots by expert id
+      const int v = ord[a];
+      int b = a - 1;
+      while (b >= 0 && topk_e[(int64_t)t * k + ord[b]] > topk_e[(int64_t)t * k + v]) {
+        ord[b + 1] = ord[b];
+        --b;
+      }
+      ord[b + 1] = v;
     }
-    ord[b + 1] = v;
-  }
-  for (int h = lane; h < H; h += 32) {
-    float acc = 0.f;
     for (int j = 0; j < k; ++j) {
       const int slot = (int)((int64_t)t * k + ord[j]);
-      acc = __fadd_rn(acc, __fmul_rn(d[(int64_t)pair_pos[slot] * H + h], topk_w[slot]));
+      s_pos[j] = pair_pos[slot];
+      s_w[j] = topk_w[slot];
     }
-    out[(int64_t)t * H + h] = acc;
+  }
+  __syncthreads();
+  for (int h = threadIdx.x * 4; h < H; h += 256 * 4) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < k; ++j) {
+      const float4 v = *reinterpret_cast<const float4*>(d + (int64_t)s_pos[j] * H + h);
+      const float w = s_w[j];
+      acc.x = __fadd_rn(acc.x, __fmul_rn(v.x, w));
+      acc.y = __fadd_rn(acc.y, __fmul_rn(v.y, w));
+      acc.z = __fadd_rn(acc.z, __fmul_rn(v.z, w));
+      acc.w = __fadd_rn(acc.w, __fmul_rn(v.w, w));
+    }
+    *reinterpret_cast<float4*>(out + (int64_t)t * H + h) = acc;
   }
 }
 
@@ -288,18 +307,28 @@ int check_common(int E, int k, int64_t T, int64_t H, int x_dtype) {
   return XM_OK;
 }
 
+template <typename XT>
+void launch_router(const XT* x, const float* gate, int64_t T, int64_t H, int E, int k, int* topk_e, float* topk_w,
+                   cudaStream_t st) {
+  const unsigned grid = (unsigned)((T + 7) / 8);   // 8 tokens (warps) per block
+  if (E <= 8)
+    k_moe_router<XT, 8><<<grid, 256, 0, st>>>(x, gate, (int)T, (int)H, E, k, topk_e, topk_w);
+  else if (E <= 16)
+    k_moe_router<XT, 16><<<grid, 256, 0, st>>>(x, gate, (int)T, (int)H, E, k, topk_e, topk_w);
+  else
+    k_moe_router<XT, kMaxExperts><<<grid, 256, 0, st>>>(x, gate, (int)T, (int)H, E, k, topk_e, topk_w);
+}
+
 // router + stable sort: topk_e/topk_w/pair_pos/sorted_tok/cnt/off in the workspace
 int route_and_sort(const void* d_x, int x_dtype, int64_t T, int64_t H, const float* d_gate, int E, int k,
                    const MoeWs& w, cudaStream_t st) {
   const int64_t P = T * k;
-  const unsigned tgrid = (unsigned)((T * 32 + 255) / 256);
   if (x_dtype == XM_DT_F32)
-    k_moe_router<float><<<tgrid, 256, 0, st>>>((const float*)d_x, d_gate, (int)T, (int)H, E, k, w.topk_e, w.topk_w);
+    launch_router<float>((const float*)d_x, d_gate, T, H, E, k, w.topk_e, w.topk_w, st);
   else if (x_dtype == XM_DT_BF16)
-    k_moe_router<__nv_bfloat16><<<tgrid, 256, 0, st>>>((const __nv_bfloat16*)d_x, d_gate, (int)T, (int)H, E, k,
-                                                         w.topk_e, w.topk_w);
+    launch_router<__nv_bfloat16>((const __nv_bfloat16*)d_x, d_gate, T, H, E, k, w.topk_e, w.topk_w, st);
   else
-    k_moe_router<__half><<<tgrid, 256, 0, st>>>((const __half*)d_x, d_gate, (int)T, (int)H, E, k, w.topk_e, w.topk_w);
+    launch_router<__half>((const __half*)d_x, d_gate, T, H, E, k, w.topk_e, w.topk_w, st);
   int rc = xm_check_launch("moe router");
   if (rc) return rc;
   k_moe_sort<<<1, 1024, 0, st>>>(w.topk_e, w.topk_w, (int)P, k, E, w.sorted_tok, w.sorted_w, w.pair_pos, w.cnt, w.off);
@@ -316,15 +345,15 @@ int run_experts(int qtype, int act, const __half* a16, const float* ascale, int6
   int rc;
   if ((rc = qgemm_grouped(qtype, a16, ascale, P, H, F, tab, cnt, off, G, max_rows, expect, g, st))) return rc;
   if ((rc = qgemm_grouped(qtype, a16, ascale, P, H, F, tab + G, cnt, off, G, max_rows, expect, u, st))) return rc;
-  const unsigned pgrid = (unsigned)((P * 32 + 255) / 256);
+  const unsigned pgrid = (unsigned)P;     // one block per row
   if (act == XM_ACT_SILU)
-    k_swiglu_prep<XM_ACT_SILU><<<pgrid, 256, 0, st>>>(g, u, (int)P, (int)F, h16, hscale);
+    k_swiglu_prep<XM_ACT_SILU><<<pgrid, kPrepThreads, 0, st>>>(g, u, (int)P, (int)F, h16, hscale);
   else if (act == XM_ACT_GELU)
-    k_swiglu_prep<XM_ACT_GELU><<<pgrid, 256, 0, st>>>(g, u, (int)P, (int)F, h16, hscale);
+    k_swiglu_prep<XM_ACT_GELU><<<pgrid, kPrepThreads, 0, st>>>(g, u, (int)P, (int)F, h16, hscale);
   else if (act == XM_ACT_RELU)
-    k_swiglu_prep<XM_ACT_RELU><<<pgrid, 256, 0, st>>>(g, u, (int)P, (int)F, h16, hscale);
+    k_swiglu_prep<XM_ACT_RELU><<<pgrid, kPrepThreads, 0, st>>>(g, u, (int)P, (int)F, h16, hscale);
   else
-    k_swiglu_prep<XM_ACT_IDENTITY><<<pgrid, 256, 0, st>>>(g, u, (int)P, (int)F, h16, hscale);
+    k_swiglu_prep<XM_ACT_IDENTITY><<<pgrid, kPrepThreads, 0, st>>>(g, u, (int)P, (int)F, h16, hscale);
   if ((rc = xm_check_launch("moe swiglu"))) return rc;
   return qgemm_grouped(qtype, h16, hscale, P, F, H, tab + 2 * G, cnt, off, G, max_rows, expect, d, st);
 }
@@ -373,6 +402,8 @@ extern "C" int xm_moe_forward(const void* d_x, int x_dtype, int64_t T, int64_t H
   if (int rc0 = check_expert_type("moe", qtype, activation, H, F)) return rc0;
   if (!d_x || !d_gate || !d_out || !d_ws || !h_w1 || !h_w2 || !h_w3)
     return xm_set_error(XM_ERR_INVALID, "moe: null pointer");
+  if (((uintptr_t)d_x | (uintptr_t)d_gate | (uintptr_t)d_out) & 15)
+    return xm_set_error(XM_ERR_INVALID, "moe: x, gate and out must be 16-byte aligned");
   if (((uintptr_t)d_ws & 255) || ws_bytes < xm_moe_workspace_size(T, H, F, E, k))
     return xm_set_error(XM_ERR_INVALID, "moe: workspace too small or not 256-byte aligned");
   for (int e = 0; e < E; ++e)
@@ -392,20 +423,19 @@ extern "C" int xm_moe_forward(const void* d_x, int x_dtype, int64_t T, int64_t H
   }
   int rc = route_and_sort(d_x, x_dtype, T, H, d_gate, E, k, w, st);
   if (rc) return rc;
-  const unsigned pgrid = (unsigned)((P * 32 + 255) / 256);
+  const unsigned pgrid = (unsigned)P;     // one block per row
   if (x_dtype == XM_DT_F32)
-    k_moe_gather_prep<float><<<pgrid, 256, 0, st>>>((const float*)d_x, w.sorted_tok, (int)P, (int)H, w.a16, w.ascale);
+    k_moe_gather_prep<float><<<pgrid, kPrepThreads, 0, st>>>((const float*)d_x, w.sorted_tok, (int)P, (int)H, w.a16, w.ascale);
   else if (x_dtype == XM_DT_BF16)
-    k_moe_gather_prep<__nv_bfloat16><<<pgrid, 256, 0, st>>>((const __nv_bfloat16*)d_x, w.sorted_tok, (int)P, (int)H,
+    k_moe_gather_prep<__nv_bfloat16><<<pgrid, kPrepThreads, 0, st>>>((const __nv_bfloat16*)d_x, w.sorted_tok, (int)P, (int)H,
                                                               w.a16, w.ascale);
   else
-    k_moe_gather_prep<__half><<<pgrid, 256, 0, st>>>((const __half*)d_x, w.sorted_tok, (int)P, (int)H, w.a16, w.ascale);
+    k_moe_gather_prep<__half><<<pgrid, kPrepThreads, 0, st>>>((const __half*)d_x, w.sorted_tok, (int)P, (int)H, w.a16, w.ascale);
   if ((rc = xm_check_launch("moe gather"))) return rc;
   if ((rc = run_experts(qtype, activation, w.a16, w.ascale, P, H, F, tab, E, w.cnt, w.off, T, w.g, w.u, w.h16, w.hscale, w.d,
                        st)))
     return rc;
-  const unsigned tgrid = (unsigned)((T * 32 + 255) / 256);
-  k_moe_combine<<<tgrid, 256, 0, st>>>(w.d, w.topk_e, w.topk_w, w.pair_pos, (int)T, (int)H, k, d_out);
+  k_moe_combine<<<(unsigned)T, 256, 0, st>>>(w.d, w.topk_e, w.topk_w, w.pair_pos, (int)T, (int)H, k, d_out);
   return xm_check_launch("moe combine");
 }
 
@@ -416,6 +446,8 @@ extern "C" int xm_moe_dispatch(const void* d_x, int x_dtype, int64_t T, int64_t 
                                int64_t F, void* d_send, int* d_cnt, void* d_ws, int64_t ws_bytes, void* stream) {
   if (int rc = check_common(E, k, T, H, x_dtype)) return rc;
   if (!d_x || !d_gate || !d_send || !d_cnt || !d_ws) return xm_set_error(XM_ERR_INVALID, "moe_dispatch: null pointer");
+  if (((uintptr_t)d_x | (uintptr_t)d_gate) & 15)
+    return xm_set_error(XM_ERR_INVALID, "moe_dispatch: x and gate must be 16-byte aligned");
   if (((uintptr_t)d_ws & 255) || ws_bytes < xm_moe_workspace_size(T, H, F, E, k))
     return xm_set_error(XM_ERR_INVALID, "moe_dispatch: workspace too small or not 256-byte aligned");
   cudaStream_t st = (cudaStream_t)stream;
@@ -456,6 +488,8 @@ extern "C" int xm_moe_experts(const void* d_rows, int x_dtype, int64_t P, int64_
   if (P == 0) return XM_OK;
   if (!d_rows || !d_cnt || !d_off || !d_out || !d_ws || !h_w1 || !h_w2 || !h_w3)
     return xm_set_error(XM_ERR_INVALID, "moe_experts: null pointer");
+  if (((uintptr_t)d_rows | (uintptr_t)d_out) & 15)
+    return xm_set_error(XM_ERR_INVALID, "moe_experts: rows and out must be 16-byte aligned");
   if (((uintptr_t)d_ws & 255) || ws_bytes < xm_moe_experts_workspace_size(P, H, F))
     return xm_set_error(XM_ERR_INVALID, "moe_experts: workspace too small or not 256-byte aligned");
   const uint8_t* tab[3 * kMaxExperts];
@@ -469,14 +503,14 @@ extern "C" int xm_moe_experts(const void* d_rows, int x_dtype, int64_t P, int64_
   }
   cudaStream_t st = (cudaStream_t)stream;
   ExpertWs w = carve_experts((uint8_t*)d_ws, P, H, F);
-  const unsigned pgrid = (unsigned)((P * 32 + 255) / 256);
+  const unsigned pgrid = (unsigned)P;     // one block per row
   if (x_dtype == XM_DT_F32)
-    k_moe_gather_prep<float><<<pgrid, 256, 0, st>>>((const float*)d_rows, nullptr, (int)P, (int)H, w.a16, w.ascale);
+    k_moe_gather_prep<float><<<pgrid, kPrepThreads, 0, st>>>((const float*)d_rows, nullptr, (int)P, (int)H, w.a16, w.ascale);
   else if (x_dtype == XM_DT_BF16)
-    k_moe_gather_prep<__nv_bfloat16><<<pgrid, 256, 0, st>>>((const __nv_bfloat16*)d_rows, nullptr, (int)P, (int)H,
+    k_moe_gather_prep<__nv_bfloat16><<<pgrid, kPrepThreads, 0, st>>>((const __nv_bfloat16*)d_rows, nullptr, (int)P, (int)H,
                                                               w.a16, w.ascale);
   else
-    k_moe_gather_prep<__half><<<pgrid, 256, 0, st>>>((const __half*)d_rows, nullptr, (int)P, (int)H, w.a16, w.ascale);
+    k_moe_gather_prep<__half><<<pgrid, kPrepThreads, 0, st>>>((const __half*)d_rows, nullptr, (int)P, (int)H, w.a16, w.ascale);
   int rc = xm_check_launch("moe_experts prep");
   if (rc) return rc;
   return run_experts(qtype, activation, w.a16, w.ascale, P, H, F, tab, G, d_cnt, d_off, std::max<int64_t>(1, max_rows), w.g, w.u,
@@ -487,9 +521,10 @@ extern "C" int xm_moe_combine(const float* d_rows, int64_t T, int64_t H, int E, 
                               float* d_out, void* stream) {
   if (int rc = check_common(E, k, T, H, XM_DT_F32)) return rc;
   if (!d_rows || !d_ws || !d_out) return xm_set_error(XM_ERR_INVALID, "moe_combine: null pointer");
+  if (((uintptr_t)d_rows | (uintptr_t)d_out) & 15)
+    return xm_set_error(XM_ERR_INVALID, "moe_combine: rows and out must be 16-byte aligned");
   MoeWs w = carve((uint8_t*)d_ws, T, H, F, E, k);
-  const unsigned tgrid = (unsigned)((T * 32 + 255) / 256);
-  k_moe_combine<<<tgrid, 256, 0, (cudaStream_t)stream>>>(d_rows, w.topk_e, w.topk_w, w.pair_pos, (int)T, (int)H, k,
+  k_moe_combine<<<(unsigned)T, 256, 0, (cudaStream_t)stream>>>(d_rows, w.topk_e, w.topk_w, w.pair_pos, (int)T, (int)H, k,
                                                           d_out);
   return xm_check_launch("moe combine");
 }

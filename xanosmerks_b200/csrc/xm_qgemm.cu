@@ -123,55 +123,45 @@ XM_DEV float byte_f(uint32_t w, int i) {
 
 // ---------------------------------------------------------------------------
 // Activation preparation: fp16 copy of pro(x) with a power-of-two scale per
-// row.  One warp per row.  rowscale[m] = 2^s with the row's max magnitude in
-// [2^14, 2^15) after division by 2^s (s may be negative for small rows).
+// row (prep_row_fp16: one block per row, vector loads).  rowscale[m] = 2^s
+// with the row's max magnitude in [2^14, 2^15) after division by 2^s (s may
+// be negative for small rows).
 // PRO is an XM_PRO_* prologue, applied in fp32 in the reference's order:
 //   XM_PRO_RMSNORM  v = (x / sqrt(mean(x^2) + eps)) * norm_w   (ops.py:115-117)
 //   XM_PRO_SWIGLU   v = silu(x[:K]) * x[K:2K]                  (forward.py:97-98)
 // `ldx` is the row pitch of x in elements.
 // ---------------------------------------------------------------------------
 template <typename XT, int PRO>
-XM_DEV float prep_value(const XT* xr, int k, int K, float rms, const float* norm_w) {
-  if constexpr (PRO == XM_PRO_RMSNORM) {
-    return (to_f32(xr[k]) / rms) * norm_w[k];
-  } else if constexpr (PRO == XM_PRO_SWIGLU) {
-    const float g = to_f32(xr[k]);
-    return g / (1.0f + expf(-g)) * to_f32(xr[K + k]);
-  } else {
-    return to_f32(xr[k]);
-  }
-}
-
-template <typename XT, int PRO>
-__global__ void __launch_bounds__(256) k_prep_rows(const XT* __restrict__ x, int M, int K, int64_t ldx,
-                                                   const float* __restrict__ norm_w, float eps,
-                                                   __half* __restrict__ x16, float* __restrict__ rowscale) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (warp >= M) return;
-  const XT* xr = x + (int64_t)warp * ldx;
+__global__ void __launch_bounds__(kPrepThreads) k_prep_rows(const XT* __restrict__ x, int M, int K, int64_t ldx,
+                                                            const float* __restrict__ norm_w, float eps,
+                                                            __half* __restrict__ x16, float* __restrict__ rowscale) {
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  const XT* xr = x + (int64_t)row * ldx;
   float rms = 1.f;
   if constexpr (PRO == XM_PRO_RMSNORM) {
     float ss = 0.f;
-    for (int k = lane; k < K; k += 32) {
-      const float v = to_f32(xr[k]);
-      ss = fmaf(v, v, ss);
+    for (int k = threadIdx.x * 4; k < K; k += kPrepThreads * 4) {
+      float v[4];
+      ld4f<XT>(xr + k, v);
+      ss = fmaf(v[0], v[0], fmaf(v[1], v[1], fmaf(v[2], v[2], fmaf(v[3], v[3], ss))));
     }
-    rms = sqrtf(warp_sum(ss) / (float)K + eps);
+    rms = sqrtf(block_sum(ss, red) / (float)K + eps);
   }
-  float amax = 0.f;
-  for (int k = lane; k < K; k += 32) amax = fmaxf(amax, fabsf(prep_value<XT, PRO>(xr, k, K, rms, norm_w)));
+  prep_row_fp16(
+      [&](int k, float (&v)[4]) {
+        ld4f<XT>(xr + k, v);
+        if constexpr (PRO == XM_PRO_RMSNORM) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  int s = 0;
-  if (amax > 0.f && amax < INFINITY) {
-    int e;
-    frexpf(amax, &e);           // amax = f * 2^e, f in [0.5, 1): amax in [2^(e-1), 2^e)
-    s = (e - 1) - 14;           // amax / 2^s in [2^14, 2^15)
-  }
-  const float inv = ldexpf(1.0f, -s);
-  __half* o = x16 + (int64_t)warp * K;
-  for (int k = lane; k < K; k += 32) o[k] = __float2half_rn(prep_value<XT, PRO>(xr, k, K, rms, norm_w) * inv);
-  if (lane == 0) rowscale[warp] = ldexpf(1.0f, s);
+          for (int i = 0; i < 4; ++i) v[i] = (v[i] / rms) * norm_w[k + i];
+        } else if constexpr (PRO == XM_PRO_SWIGLU) {
+          float u[4];
+          ld4f<XT>(xr + K + k, u);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) v[i] = v[i] / (1.0f + expf(-v[i])) * u[i];
+        }
+      },
+      K, x16 + (int64_t)row * K, rowscale + row, red);
 }
 
 // Plain RMSNorm of rows (one warp per row), fp32 out: the norm of
@@ -1262,14 +1252,17 @@ namespace {
 template <typename XT>
 void launch_prep(const void* x, int prologue, int64_t m, int64_t k, int64_t ldx, const float* norm_w, float eps,
                  __half* x16, float* rowscale, cudaStream_t st) {
-  const unsigned pgrid = (unsigned)((m * 32 + 255) / 256);
+  const unsigned pgrid = (unsigned)m;        // one block per row
   const XT* xt = (const XT*)x;
   if (prologue == XM_PRO_RMSNORM)
-    k_prep_rows<XT, XM_PRO_RMSNORM><<<pgrid, 256, 0, st>>>(xt, (int)m, (int)k, ldx, norm_w, eps, x16, rowscale);
+    k_prep_rows<XT, XM_PRO_RMSNORM><<<pgrid, kPrepThreads, 0, st>>>(xt, (int)m, (int)k, ldx, norm_w, eps, x16,
+                                                                    rowscale);
   else if (prologue == XM_PRO_SWIGLU)
-    k_prep_rows<XT, XM_PRO_SWIGLU><<<pgrid, 256, 0, st>>>(xt, (int)m, (int)k, ldx, norm_w, eps, x16, rowscale);
+    k_prep_rows<XT, XM_PRO_SWIGLU><<<pgrid, kPrepThreads, 0, st>>>(xt, (int)m, (int)k, ldx, norm_w, eps, x16,
+                                                                   rowscale);
   else
-    k_prep_rows<XT, XM_PRO_NONE><<<pgrid, 256, 0, st>>>(xt, (int)m, (int)k, ldx, norm_w, eps, x16, rowscale);
+    k_prep_rows<XT, XM_PRO_NONE><<<pgrid, kPrepThreads, 0, st>>>(xt, (int)m, (int)k, ldx, norm_w, eps, x16,
+                                                                 rowscale);
 }
 }  // namespace
 
