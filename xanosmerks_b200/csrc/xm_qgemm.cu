@@ -436,15 +436,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 // only its own halves from shared memory.  Tiles go round-robin over the
 // pairs (order: pair_tile).
 //
-// Per CTA (2 + 16 + 4 warps):
-//   warp 0      TMA producer: raw block records of the CTA's weight rows, one
-//               256-wide K column per stage (ColGeom<T>: a box of BB bytes x
-//               BN/2 rows per N half, starting at the column's first byte
-//               rounded down to 16 -- TMA's alignment rule -- and wide enough
-//               for the column at any of its offsets), and the fp16
-//               activation box (64 K x 128 rows, 128-byte swizzle) of every
-//               64-wide K step.  Rank 1's activation box completes on rank 0's
-//               barrier (cta_group::2 form of the tensor load; no multicast).
+// Per CTA (2 + 16 + 4 + 1 warps):
+//   warp 0      TMA producer of the fp16 activation box (64 K x 128 rows,
+//               128-byte swizzle) of every 64-wide K step.  Rank 1's
+//               activation box completes on rank 0's barrier (cta_group::2
+//               form of the tensor load; no multicast).
+//   warp 22     TMA producer of the raw block records of the CTA's weight
+//               rows, one 256-wide K column per stage (ColGeom<T>: a box of BB
+//               bytes x BN/2 rows per N half, starting at the column's first
+//               byte rounded down to 16 -- TMA's alignment rule -- and wide
+//               enough for the column at any of its offsets); a thread of its
+//               own so that the next column is requested as soon as a raw
+//               slot is free.
 //   warp 1      TMEM allocation (both ranks); rank 0 issues the MMAs.
 //   warps 2-17  decode, two groups of 8 warps taking turns by K step: one
 //               thread per (row, 32-weight sub-block) item, from the staged
@@ -468,7 +471,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 // cluster-scope release costs ~200 ns per arrival here against ~50 ns.
 // ---------------------------------------------------------------------------
 constexpr int kPairEpiWarps = 4;
-constexpr int pair_threads(int dw) { return (2 + dw + kPairEpiWarps) * 32; }
+// warps: TMA producer of the activation tiles, MMA issuer, DW decode warps,
+// the epilogue warps, and the TMA producer of the raw weight records
+constexpr int pair_threads(int dw) { return (2 + dw + kPairEpiWarps + 1) * 32; }
 constexpr int kMaxRawStages = 2;
 constexpr int kEpiTileFloats = 32 * 33;        // per-warp padded 32 x 32 staging tile
 
@@ -487,6 +492,133 @@ struct ColGeom {
   static constexpr int BB = (CB + MIS + 15) / 16 * 16;
   static_assert(BB / 2 <= 256, "TMA box width");
 };
+
+// NW consecutive 32-bit words at a 2-byte-aligned shared address: NW + 1
+// aligned loads joined by funnel shifts (shift 0 or 16).
+template <int NW>
+XM_DEV void smem_words(const uint8_t* p, uint32_t (&w)[NW]) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uint32_t* base = reinterpret_cast<const uint32_t*>(a & ~(uintptr_t)3);
+  const uint32_t sh = (uint32_t)(a & 3) * 8;
+  uint32_t prev = base[0];
+#pragma unroll
+  for (int i = 0; i < NW; ++i) {
+    const uint32_t next = base[i + 1];
+    w[i] = __funnelshift_r(prev, next, sh);
+    prev = next;
+  }
+}
+
+// Four bytes of w (codes b0..b3) as exact floats b - bias, in two pairs:
+// 2^23 + b by byte permute into the exponent pattern, minus (2^23 + bias).
+XM_DEV void bytes_minus(uint32_t w, float bias, float2& lo, float2& hi) {
+  const float2 mg = make_float2(-(8388608.0f + bias), -(8388608.0f + bias));
+  lo = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7650u)),
+                              __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7651u))), mg);
+  hi = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7652u)),
+                              __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7653u))), mg);
+}
+
+XM_DEV uint32_t half2_bits(float2 v) {
+  const __half2 h = __floats2half2_rn(v.x, v.y);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Q6_K item (gguf_dequant.py:392-436): weights 64j + 32h + l, l = 0..31, of the
+// record at `rec` (2-byte aligned): half hh = j/2 of the super-block, quarter
+// i = 2(j%2) + h; code = nibble i/2 of ql[64hh + 32(i%2) + l] | bits 2i..2i+1 of
+// qh[32hh + l] << 4; value (d * sc[8hh + 2i + l/16]) * (code - 32) -- an exact
+// product, rounded once to fp16 as the reference's astype does.
+XM_DEV void decode_q6k_item(const uint8_t* rec, int j, int h, uint8_t* row, int n) {
+  const int hh = j >> 1, i = 2 * (j & 1) + h;
+  uint32_t ql[8], qh[8];
+  smem_words<8>(rec + 64 * hh + 32 * (i & 1), ql);
+  smem_words<8>(rec + 128 + 32 * hh, qh);
+  const float d = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(rec + 208)));
+  const float ds0 = d * (float)(int8_t)rec[192 + 8 * hh + 2 * i];       // exact (11-bit x 8-bit)
+  const float ds1 = d * (float)(int8_t)rec[192 + 8 * hh + 2 * i + 1];
+  const int nsh = 4 * (i >> 1), hsh = 2 * i;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {               // chunk c: weights 8c .. 8c+7 of the item (words 2c, 2c+1)
+    const float ds = c < 2 ? ds0 : ds1;
+    const float2 dd = make_float2(ds, ds);
+    uint32_t hv[4];
+#pragma unroll
+    for (int wv = 0; wv < 2; ++wv) {
+      const int w = 2 * c + wv;
+      const uint32_t q = ((ql[w] >> nsh) & 0x0F0F0F0Fu) | (((qh[w] >> hsh) & 0x03030303u) << 4);
+      float2 lo, hi;
+      bytes_minus(q, 32.0f, lo, hi);
+      hv[2 * wv] = half2_bits(__fmul2_rn(lo, dd));
+      hv[2 * wv + 1] = half2_bits(__fmul2_rn(hi, dd));
+    }
+    const int chunk = 4 * h + c;
+    *reinterpret_cast<uint4*>(row + ((chunk ^ (n & 7)) << 4)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+  }
+}
+
+// Q5_K item (gguf_dequant.py:347-386, with the reference's high-bit layout):
+// sub-block s = 2j + h, weights l = 0..31: code = nibble h of qs[48 + 32j + l]
+// + 16 * (bit l of the little-endian u32 at 16 + 4j); value (d*sc_s)*code -
+// dmin*mn_s with one rounding (the products are exact).  The record is
+// 16-byte aligned (176-byte records, 16-byte aligned columns).
+XM_DEV void decode_q5k_item(const uint8_t* rec, int j, int h, uint8_t* row, int n) {
+  const uint4 hd = *reinterpret_cast<const uint4*>(rec);
+  const int sub = 2 * j + h;
+  const uint32_t A = hd.y, B = hd.z, C = hd.w;
+  const uint32_t scw = sub < 4 ? (A & 0x3F3F3F3Fu) : ((C & 0x0F0F0F0Fu) | ((A >> 2) & 0x30303030u));
+  const uint32_t mnw = sub < 4 ? (B & 0x3F3F3F3Fu) : (((C >> 4) & 0x0F0F0F0Fu) | ((B >> 2) & 0x30303030u));
+  const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFF)));
+  const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
+  const float d1 = __fmul_rn(d, byte_f(scw, sub & 3));
+  const float m1 = __fmul_rn(dmin, byte_f(mnw, sub & 3));
+  const float2 dd = make_float2(d1, d1), mm = make_float2(-m1, -m1);
+  const uint32_t qh32 = *reinterpret_cast<const uint32_t*>(rec + 16 + 4 * j);
+  const uint4 q0 = *reinterpret_cast<const uint4*>(rec + 48 + 32 * j);
+  const uint4 q1 = *reinterpret_cast<const uint4*>(rec + 64 + 32 * j);
+  const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+  const int sh = 4 * h;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t hv[4];
+#pragma unroll
+    for (int wv = 0; wv < 2; ++wv) {
+      const int w = 2 * c + wv;
+      // bits 4w..4w+3 of the high-bit word -> bit 4 of bytes 0..3 (the partial products do not overlap)
+      const uint32_t fifth = (((qh32 >> (4 * w)) & 0xFu) * 0x02040810u) & 0x10101010u;
+      const uint32_t q = ((qw[w] >> sh) & 0x0F0F0F0Fu) | fifth;
+      float2 lo, hi;
+      bytes_minus(q, 0.0f, lo, hi);
+      hv[2 * wv] = half2_bits(__ffma2_rn(dd, lo, mm));
+      hv[2 * wv + 1] = half2_bits(__ffma2_rn(dd, hi, mm));
+    }
+    const int chunk = 4 * h + c;
+    *reinterpret_cast<uint4*>(row + ((chunk ^ (n & 7)) << 4)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+  }
+}
+
+// Q8_0 item (gguf_dequant.py:143-156): record 2j + h of the 256-wide column
+// (34 bytes, 2-byte aligned): int8(q) * d, an exact product rounded once.
+XM_DEV void decode_q8_0_item(const uint8_t* col, int j, int h, uint8_t* row, int n) {
+  const uint8_t* rec = col + (2 * j + h) * 34;
+  const float d = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(rec)));
+  const float2 dd = make_float2(d, d);
+  uint32_t qw[8];
+  smem_words<8>(rec + 2, qw);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t hv[4];
+#pragma unroll
+    for (int wv = 0; wv < 2; ++wv) {
+      float2 lo, hi;
+      bytes_minus(qw[2 * c + wv] ^ 0x80808080u, 128.0f, lo, hi);   // signed byte b: (b + 128) - 128
+      hv[2 * wv] = half2_bits(__fmul2_rn(lo, dd));
+      hv[2 * wv + 1] = half2_bits(__fmul2_rn(hi, dd));
+    }
+    const int chunk = 4 * h + c;
+    *reinterpret_cast<uint4*>(row + ((chunk ^ (n & 7)) << 4)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+  }
+}
 
 // One decode item of a type without a hand-tuned decoder: weights 32h .. 32h+31
 // of K step j (64 weights) of one row, from the staged column `col`, rounded
@@ -689,24 +821,17 @@ __global__ void __launch_bounds__(pair_threads(DW), 1)
   // which run on single threads).  Waits on an "empty" barrier use the
   // opposite parity, so the first lap passes at once.
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- TMA producer: activation tiles ----------------
     if (lane == 0) {
       grid_dep_wait();
       const uint32_t leader_ofull = mapa_shared(smem_u32(&ctl->ofull[0]), 0);
-      uint32_t s = 0, ph = 0, rs = 0, rph = 0;
+      uint32_t s = 0, ph = 0;
       for (int t = pair; t < NT; t += npairs) {
         PairTile pt;
         if (!pair_tile(pw, t, M, TM, TN, width, pt)) continue;
-        const CUtensorMap* wmap = &pw.map[NMAP == 1 ? 0 : pt.g];
-        const int am = pt.am0 + (int)rank * 128, wn = pt.col0 + (int)rank * hb;
+        const int am = pt.am0 + (int)rank * 128;
         int ka = 0;
         for (int kb = 0; kb < KB; ++kb) {
-          pair_wait(&ctl->wempty[rs], rph ^ 1);
-          mbar_arrive_expect_tx(&ctl->wfull[rs], (uint32_t)wstage);
-          const int wx = ((kb * CG::CB) & ~15) >> 1;   // 16-byte aligned start, in 16-bit elements
-          for (int h = 0; h < NH; ++h)
-            tma_load_2d(sW + rs * wstage + h * hb * CG::BB, wmap, wx, wn + h * BN, &ctl->wfull[rs]);
-          if (++rs == (uint32_t)RW) { rs = 0; rph ^= 1; }
           for (int j = 0; j < 4; ++j, ka += kBK) {
             pair_wait(&ctl->oempty[s], ph ^ 1);
             if (rank == 0) {
@@ -793,6 +918,12 @@ __global__ void __launch_bounds__(pair_threads(DW), 1)
                 const uint4 q1 = *reinterpret_cast<const uint4*>(rec + 32 + 32 * j);
                 const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
                 decode_part<4>(hd[p], qw, h, j, 0, dst, rr);
+              } else if constexpr (T == T_Q6_K) {
+                decode_q6k_item(rec, j, h, dst, rr);
+              } else if constexpr (T == T_Q5_K) {
+                decode_q5k_item(rec, j, h, dst, rr);
+              } else if constexpr (T == T_Q8_0) {
+                decode_q8_0_item(rec, j, h, dst, rr);
               } else {
                 decode_item_generic<T>(rec, j, h, dst, rr);
               }
@@ -812,6 +943,28 @@ __global__ void __launch_bounds__(pair_threads(DW), 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&ctl->wempty[rs]);
         if (++rs == (uint32_t)RW) { rs = 0; rph ^= 1; }
+      }
+    }
+  } else if (warp == 2 + DW + kPairEpiWarps) {
+    // ---------------- TMA producer: raw weight records ----------------
+    // A thread of its own, so that the next super-block column is requested
+    // as soon as a raw slot is free rather than behind the activation tiles
+    // (whose loads wait for the MMA to release operand stages).
+    if (lane == 0) {
+      uint32_t rs = 0, rph = 0;
+      for (int t = pair; t < NT; t += npairs) {
+        PairTile pt;
+        if (!pair_tile(pw, t, M, TM, TN, width, pt)) continue;
+        const CUtensorMap* wmap = &pw.map[NMAP == 1 ? 0 : pt.g];
+        const int wn = pt.col0 + (int)rank * hb;
+        for (int kb = 0; kb < KB; ++kb) {
+          pair_wait(&ctl->wempty[rs], rph ^ 1);
+          mbar_arrive_expect_tx(&ctl->wfull[rs], (uint32_t)wstage);
+          const int wx = ((kb * CG::CB) & ~15) >> 1;   // 16-byte aligned start, in 16-bit elements
+          for (int h = 0; h < NH; ++h)
+            tma_load_2d(sW + rs * wstage + h * hb * CG::BB, wmap, wx, wn + h * BN, &ctl->wfull[rs]);
+          if (++rs == (uint32_t)RW) { rs = 0; rph ^= 1; }
+        }
       }
     }
   } else {

@@ -361,6 +361,7 @@ constexpr int kWsThreads = (kWsConsumers + 1) * 32;
 // 171 KB) is in flight before the consumers finish their activation prologue
 constexpr int kWsSlots = 20;
 constexpr int kWsRowsPerSlot = 4;
+constexpr int kWsEarlyChunks = 6;  // copies issued before the activation row arrives
 constexpr int kRowBytes4096 = 16 * 144;
 constexpr int kWsSlotBytes = kWsRowsPerSlot * kRowBytes4096;
 // slots | lane-major split | barriers and counters | (fused form) the raw fp32/bf16 row of x
@@ -518,9 +519,15 @@ __global__ void __launch_bounds__(kWsThreads, 1) k_qgemv_q4k_k4096_m1(const uint
   __syncthreads();
 
   if (warp == kWsConsumers) {
-    // producer: weights only, so no wait on the preceding kernel
+    // producer: the first kWsEarlyChunks copies need no wait on the preceding
+    // kernel (weights only); the rest are queued behind the activation row,
+    // so that the row's copy does not wait behind the whole weight stream
     if (lane == 0) {
       for (int q = 0; q < nchunks; ++q) {
+        if (q == kWsEarlyChunks) {
+          grid_dep_wait();
+          mbar_wait_bounded(xbar, 0);   // the activation (or its split) has landed
+        }
         const int slot = q % kWsSlots;
         if (q >= kWsSlots) mbar_wait_bounded(&empty[slot], (uint32_t)(((q / kWsSlots) - 1) & 1));
         *(volatile int*)&slot_chunk[slot] = q;   // the previous lap of this slot is fully consumed
