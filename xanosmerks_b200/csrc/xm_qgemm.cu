@@ -15,12 +15,16 @@
 // fp32 `x @ W.T` only in summation order (and, for fp32 x, in x's fp16
 // rounding).
 //
-// Two kernels:
-//  * k_qgemm_pair<T> (the default, every block type T): persistent CTA pairs
-//    on tcgen05 cta_group::2 (M = 256 per MMA), raw block records staged by
-//    TMA and decoded by two interleaved groups of decode warps,
-//    double-buffered TMEM accumulators with dedicated epilogue warps; dense
-//    and grouped (MoE) modes.  Its own comment block below has the details.
+// Three kernels:
+//  * k_qgemm_tm<T> (the default, every block type T): persistent CTA pairs on
+//    tcgen05 cta_group::2 computing y^T = W x^T: the decoded weights are the
+//    M = 256 operand, written by decode warps straight into tensor memory,
+//    the activations the N operand, TMA-staged in shared memory; the
+//    epilogue writes y with bulk tensor stores.  Dense and grouped (MoE)
+//    modes.  Its own comment block below has the details.
+//  * k_qgemm_pair<T>: the same pairs with the activations as the M operand
+//    and the decoded weights staged in shared memory; used when a device
+//    cannot hold the tensor-memory-A kernel.
 //  * k_qgemm_q4k_tc (Q4_K only): one CTA per output tile of MT*128 rows x BN
 //    columns, used when a device cannot hold a CTA pair of the chosen size:
 //   warp 0      TMA producer of the activation tiles (fp16, 128-byte swizzle,
@@ -33,6 +37,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 #include "xm_internal.h"
@@ -482,14 +487,18 @@ constexpr int kEpiTileFloats = 32 * 33;        // per-warp padded 32 x 32 stagin
 // starts at byte kb*CB of its row, which is 16-byte aligned only when CB is a
 // multiple of 16; its offset inside the 16-byte unit is a multiple of
 // gcd(CB, 16), at most MIS.  The TMA box (BB bytes per row, 16-bit elements)
-// starts at the rounded-down address and covers CB + MIS bytes.
+// starts at the rounded-down address and covers CB + MIS bytes, rounded up
+// to an odd number of 16-byte units: rows BB bytes apart then fall on
+// distinct 16-byte bank groups for 8 consecutive rows, so the decoders'
+// 16-byte shared loads (one row per thread) are conflict-free.
 constexpr int gcd16(int v) { return (v & 15) == 0 ? 16 : (v & 7) == 0 ? 8 : (v & 3) == 0 ? 4 : (v & 1) == 0 ? 2 : 1; }
 template <int T>
 struct ColGeom {
   static constexpr int QK = QT<T>::QK, REC = QT<T>::REC;
   static constexpr int CB = REC * (256 / QK);
   static constexpr int MIS = (CB & 15) == 0 ? 0 : 16 - gcd16(CB);
-  static constexpr int BB = (CB + MIS + 15) / 16 * 16;
+  static constexpr int BB0 = (CB + MIS + 15) / 16 * 16;
+  static constexpr int BB = (BB0 / 16) % 2 ? BB0 : BB0 + 16;
   static_assert(BB / 2 <= 256, "TMA box width");
 };
 
@@ -507,6 +516,40 @@ XM_DEV void smem_words(const uint8_t* p, uint32_t (&w)[NW]) {
     w[i] = __funnelshift_r(prev, next, sh);
     prev = next;
   }
+}
+
+// NW consecutive 32-bit words at a 2-byte-aligned shared address whose
+// offset in its 16-byte unit (p & 15) is the same for every thread of the
+// warp: 16-byte loads of the units that hold them, then funnel shifts.
+template <int NW>
+XM_DEV void smem_words16(const uint8_t* p, uint32_t (&w)[NW]) {
+  constexpr int NU = (NW * 4 + 15 + 15) / 16;     // 16-byte units that can hold NW words at any offset
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  const uint4* base = reinterpret_cast<const uint4*>(a & ~(uintptr_t)15);
+  uint32_t u[NU * 4];
+#pragma unroll
+  for (int i = 0; i < NU; ++i) {
+    const uint4 v = base[i];
+    u[4 * i] = v.x;
+    u[4 * i + 1] = v.y;
+    u[4 * i + 2] = v.z;
+    u[4 * i + 3] = v.w;
+  }
+  const uint32_t sh = (uint32_t)(a & 3) * 8;
+  const int o = (int)((a >> 2) & 3);
+  // o is warp-uniform: one branch, each with constant register indices
+#define XM_SW16(O)                                                          \
+  _Pragma("unroll") for (int i = 0; i < NW; ++i) w[i] = __funnelshift_r(u[(O) + i], u[(O) + i + 1], sh)
+  if (o == 0) {
+    XM_SW16(0);
+  } else if (o == 1) {
+    XM_SW16(1);
+  } else if (o == 2) {
+    XM_SW16(2);
+  } else {
+    XM_SW16(3);
+  }
+#undef XM_SW16
 }
 
 // Four bytes of w (codes b0..b3) as exact floats b - bias, in two pairs:
@@ -1022,6 +1065,525 @@ __global__ void __launch_bounds__(pair_threads(DW), 1)
 }
 
 // ---------------------------------------------------------------------------
+// Tensor-memory-A GEMM (CTA pairs): the decoded weights never touch shared
+// memory.  The product is computed transposed, D[feature][token] =
+// sum_k W[feature][k] * x[token][k]: the weights are the A operand of
+// tcgen05.mma, written by the decode warps straight into tensor memory with
+// tcgen05.st (lane = weight row, 32-bit column = two consecutive K values),
+// and the fp16 activation is the B operand, TMA-staged in shared memory
+// (128-byte swizzle, K-major).  Per K step and CTA, shared memory then carries
+// only the activation tile and the raw weight records; in the CTA-pair kernel
+// above it also carries the decoded B tile (written by the decode warps and
+// read by both tensor cores), which measured as the limit of that kernel.
+//
+// A pair covers 256 weight rows (rank r: rows 128r..128r+127 of the tile, in
+// its own tensor memory) and NT tokens (rank r stages tokens NT/2 r ..
+// NT/2 (r+1) - 1 of the B operand).  One pipeline stage is 128 K values: 8
+// MMAs (K = 16 each) per barrier wait, since a wait on the issuing thread
+// costs about as much as issuing two MMAs and small-N MMAs are issue-bound.
+// Tensor memory (512 columns per CTA): nacc accumulators of NT columns, then
+// S stages of 64 columns of A (128 K values x 128 rows).
+//
+// Warps (24 per CTA):
+//   0        TMA producer of the activation tiles, two 64-K boxes per stage
+//            (rank 1's complete on rank 0's barrier, cta_group::2 form of the
+//            tensor load; no multicast)
+//   1        tensor-memory allocation (both ranks); rank 0 issues the MMAs
+//   2        TMA producer of the raw weight records (one 256-wide K column of
+//            128 rows per ring slot, ColGeom<T> boxes)
+//   3        idle
+//   4-19     decode: warp 4 + 8g + 4h + q decodes K step j = 2g + h (64
+//            weights) of every 256-wide column for the rows of lane quarter q
+//            (the tensor-memory lanes warp q (mod 4) may access): stage 2c + g
+//            of column c, its A columns 32h .. 32h + 31, two tcgen05.st of 16
+//            columns per thread (one row each)
+//   20-23    epilogue: tcgen05.ld of 32 tokens per thread (its row = one
+//            output feature), row scale of each token, bias, bulk tensor
+//            stores of 32 x 32 boxes
+// Barriers (all waits bounded):
+//   ofull[S]   (rank 0) both producers' expect-tx arrivals and TMA bytes + the
+//              8 + 8 decode warps of the group that owns the stage
+//   oempty[S]  MMA commit, multicast to both CTAs (frees the B stage and the A
+//              columns of the stage)
+//   wfull/wempty[RW]  raw record ring (TMA bytes / 16 decode-warp arrivals)
+//   acc_full[2], acc_empty[2] as in the CTA-pair kernel
+// ---------------------------------------------------------------------------
+constexpr int kTmDecodeWarps = 16;
+constexpr int kTmThreads = (4 + kTmDecodeWarps + kPairEpiWarps) * 32;
+constexpr int kTmMaxStages = 6;
+constexpr int kTmStageK = 128;              // K values per pipeline stage
+constexpr int kTmRows = 128;                // weight rows per CTA
+constexpr int kTmEpiBox = 32 * 32;          // fp32 output box: 32 tokens x 32 features
+
+struct TmSmem {
+  uint64_t wfull[kMaxRawStages], wempty[kMaxRawStages];
+  uint64_t ofull[kTmMaxStages], oempty[kTmMaxStages];
+  uint64_t acc_full[2], acc_empty[2];
+  uint32_t tmem_base;
+};
+
+XM_DEV void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+XM_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Bulk tensor store / reduce-add of a shared-memory box to global memory, and
+// the bulk-group waits that guard the reuse of the box.
+XM_DEV void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+               ::"l"(map), "r"(c0), "r"(c1), "r"(smem_u32(src))
+               : "memory");
+}
+XM_DEV void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];"
+               ::"l"(map), "r"(c0), "r"(c1), "r"(smem_u32(src))
+               : "memory");
+}
+XM_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+XM_DEV void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+XM_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// D[tmem] (+)= A[tmem] * B[smem descriptor], both CTAs of the pair
+XM_DEV void tc2_mma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// The 8 MMAs of one 128-K stage (K = 16 each) in one instruction block, so
+// that the issuing thread, which shares its scheduler with decode warps, runs
+// as few instructions as possible: A columns a + 8k, B descriptors {blo +
+// boff_k, bhi} (the low word holds the start address field, which the
+// offsets never carry out of), accumulate into D except for the first MMA
+// when `first` is set.
+XM_DEV void tc2_mma_stage128(uint32_t d, uint32_t a, uint32_t blo, uint32_t bhi, uint32_t bh, uint32_t idesc,
+                             uint32_t first) {
+  asm volatile(
+      "{\n"
+      " .reg .pred p0, p1;\n"
+      " .reg .b32 l;\n"
+      " .reg .b64 bd;\n"
+      " setp.eq.b32 p0, %6, 0;\n"
+      " setp.eq.b32 p1, %6, %6;\n"
+      " mov.b64 bd, {%2, %3};\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], bd, %5, p0;\n"
+      " add.u32 l, %2, 2;\n mov.b64 bd, {l, %3};\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], [%7], bd, %5, p1;\n"
+      " add.u32 l, %2, 4;\n mov.b64 bd, {l, %3};\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], [%8], bd, %5, p1;\n"
+      " add.u32 l, %2, 6;\n mov.b64 bd, {l, %3};\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], [%9], bd, %5, p1;\n"
+      " add.u32 l, %2, %4;\n mov.b64 bd, {l, %3};\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], [%10], bd, %5, p1;\n"
+      " add.u32 l, l, 2;\n mov.b64 bd, {l, %3};\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], [%11], bd, %5, p1;\n"
+      " add.u32 l, l, 2;\n mov.b64 bd, {l, %3};\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], [%12], bd, %5, p1;\n"
+      " add.u32 l, l, 2;\n mov.b64 bd, {l, %3};\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], [%13], bd, %5, p1;\n"
+      "}"
+      ::"r"(d), "r"(a), "r"(blo), "r"(bhi), "r"(bh), "r"(idesc), "r"(first), "r"(a + 8u), "r"(a + 16u),
+        "r"(a + 24u), "r"(a + 32u), "r"(a + 40u), "r"(a + 48u), "r"(a + 56u)
+      : "memory");
+}
+
+// Register forms of the item decoders: hv[4c + t] = the fp16 pair of weights
+// (8c + 2t, 8c + 2t + 1) of item h (weights 32h .. 32h+31 of K step j).
+XM_DEV void q4k_item_regs(const uint8_t* rec, int j, int h, uint32_t (&hv)[16]) {
+  const uint4 hd = *reinterpret_cast<const uint4*>(rec);
+  const uint4 q0 = *reinterpret_cast<const uint4*>(rec + 16 + 32 * j);
+  const uint4 q1 = *reinterpret_cast<const uint4*>(rec + 32 + 32 * j);
+  const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+  const uint32_t A = hd.y, B = hd.z, C = hd.w;
+  const int sub = 2 * j + h;
+  const uint32_t scw = sub < 4 ? (A & 0x3F3F3F3Fu) : ((C & 0x0F0F0F0Fu) | ((A >> 2) & 0x30303030u));
+  const uint32_t mnw = sub < 4 ? (B & 0x3F3F3F3Fu) : (((C >> 4) & 0x0F0F0F0Fu) | ((B >> 2) & 0x30303030u));
+  const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFF)));
+  const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
+  const float d1 = __fmul_rn(d, byte_f(scw, sub & 3));       // exact (11-bit x 6-bit)
+  const float m1 = __fmul_rn(dmin, byte_f(mnw, sub & 3));
+  const float2 dd = make_float2(d1, d1), mm = make_float2(-m1, -m1);
+  const int sh = 4 * h;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    float2 lo, hi;
+    bytes_minus((qw[w] >> sh) & 0x0F0F0F0Fu, 0.0f, lo, hi);
+    // d1*q is exact, so one rounding of d1*q - m1 is the reference's fp32 value
+    hv[2 * w] = half2_bits(__ffma2_rn(dd, lo, mm));
+    hv[2 * w + 1] = half2_bits(__ffma2_rn(dd, hi, mm));
+  }
+}
+
+XM_DEV void q6k_item_regs(const uint8_t* rec, int j, int h, uint32_t (&hv)[16]) {
+  const int hh = j >> 1, i = 2 * (j & 1) + h;
+  uint32_t ql[8], qh[8];
+  smem_words16<8>(rec + 64 * hh + 32 * (i & 1), ql);
+  smem_words16<8>(rec + 128 + 32 * hh, qh);
+  const float d = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(rec + 208)));
+  const float ds0 = d * (float)(int8_t)rec[192 + 8 * hh + 2 * i];       // exact (11-bit x 8-bit)
+  const float ds1 = d * (float)(int8_t)rec[192 + 8 * hh + 2 * i + 1];
+  const int nsh = 4 * (i >> 1), hsh = 2 * i;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    const float ds = w < 4 ? ds0 : ds1;       // weights 0-15 and 16-31 of the item
+    const float2 dd = make_float2(ds, ds);
+    const uint32_t q = ((ql[w] >> nsh) & 0x0F0F0F0Fu) | (((qh[w] >> hsh) & 0x03030303u) << 4);
+    float2 lo, hi;
+    bytes_minus(q, 32.0f, lo, hi);
+    hv[2 * w] = half2_bits(__fmul2_rn(lo, dd));
+    hv[2 * w + 1] = half2_bits(__fmul2_rn(hi, dd));
+  }
+}
+
+XM_DEV void q5k_item_regs(const uint8_t* rec, int j, int h, uint32_t (&hv)[16]) {
+  const uint4 hd = *reinterpret_cast<const uint4*>(rec);
+  const int sub = 2 * j + h;
+  const uint32_t A = hd.y, B = hd.z, C = hd.w;
+  const uint32_t scw = sub < 4 ? (A & 0x3F3F3F3Fu) : ((C & 0x0F0F0F0Fu) | ((A >> 2) & 0x30303030u));
+  const uint32_t mnw = sub < 4 ? (B & 0x3F3F3F3Fu) : (((C >> 4) & 0x0F0F0F0Fu) | ((B >> 2) & 0x30303030u));
+  const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFF)));
+  const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
+  const float d1 = __fmul_rn(d, byte_f(scw, sub & 3));
+  const float m1 = __fmul_rn(dmin, byte_f(mnw, sub & 3));
+  const float2 dd = make_float2(d1, d1), mm = make_float2(-m1, -m1);
+  const uint32_t qh32 = *reinterpret_cast<const uint32_t*>(rec + 16 + 4 * j);
+  const uint4 q0 = *reinterpret_cast<const uint4*>(rec + 48 + 32 * j);
+  const uint4 q1 = *reinterpret_cast<const uint4*>(rec + 64 + 32 * j);
+  const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+  const int sh = 4 * h;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    const uint32_t fifth = (((qh32 >> (4 * w)) & 0xFu) * 0x02040810u) & 0x10101010u;
+    float2 lo, hi;
+    bytes_minus(((qw[w] >> sh) & 0x0F0F0F0Fu) | fifth, 0.0f, lo, hi);
+    hv[2 * w] = half2_bits(__ffma2_rn(dd, lo, mm));
+    hv[2 * w + 1] = half2_bits(__ffma2_rn(dd, hi, mm));
+  }
+}
+
+XM_DEV void q8_0_item_regs(const uint8_t* col, int j, int h, uint32_t (&hv)[16]) {
+  const uint8_t* rec = col + (2 * j + h) * 34;
+  const float d = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(rec)));
+  const float2 dd = make_float2(d, d);
+  uint32_t qw[8];
+  smem_words16<8>(rec + 2, qw);
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    float2 lo, hi;
+    bytes_minus(qw[w] ^ 0x80808080u, 128.0f, lo, hi);   // signed byte b: (b + 128) - 128
+    hv[2 * w] = half2_bits(__fmul2_rn(lo, dd));
+    hv[2 * w + 1] = half2_bits(__fmul2_rn(hi, dd));
+  }
+}
+
+template <int T>
+XM_DEV void generic_item_regs(const uint8_t* col, int j, int h, uint32_t (&hv)[16]) {
+  using Q = QT<T>;
+  const uint8_t* rec = Q::QK == 256 ? col : col + (2 * j + h) * Q::REC;
+  const int e0 = Q::QK == 256 ? 64 * j + 32 * h : 0;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    float v[8];
+    Q::decode8(rec, e0 + 8 * c, v);
+#pragma unroll
+    for (int p = 0; p < 4; ++p) hv[4 * c + p] = half2_bits(make_float2(v[2 * p], v[2 * p + 1]));
+  }
+}
+
+template <int T>
+XM_DEV void item_regs(const uint8_t* rec, int j, int h, uint32_t (&hv)[16]) {
+  if constexpr (T == T_Q4_K) q4k_item_regs(rec, j, h, hv);
+  else if constexpr (T == T_Q6_K) q6k_item_regs(rec, j, h, hv);
+  else if constexpr (T == T_Q5_K) q5k_item_regs(rec, j, h, hv);
+  else if constexpr (T == T_Q8_0) q8_0_item_regs(rec, j, h, hv);
+  else generic_item_regs<T>(rec, j, h, hv);
+}
+
+// Tile t of the tensor-memory-A kernel: token tile (fastest, so that the
+// pairs that run together share a weight tile in L2) and 256-row weight tile.
+template <int NMAP>
+XM_DEV bool tm_tile(const PairW<NMAP>& pw, int t, int M, int TM, int TW, int NT, PairTile& pt) {
+  if (NMAP == 1) {
+    pt.g = 0;
+    pt.am0 = (t % TM) * NT;
+    pt.mhi = M;
+    pt.col0 = (t / TM) * 256;
+    return true;
+  }
+  const int wt = t % TW, r = t / TW;
+  const int mt = r % TM, g = r / TM;
+  const int lo = pw.off[g], cnt = pw.cnt[g];
+  pt.g = g;
+  pt.am0 = lo + mt * NT;
+  pt.mhi = lo + cnt;
+  pt.col0 = wt * 256;
+  return mt * NT < cnt;
+}
+
+template <int T, int NMAP>
+__global__ void __launch_bounds__(kTmThreads, 1)
+    k_qgemm_tm(const __grid_constant__ CUtensorMap map_b, const __grid_constant__ PairW<NMAP> pw,
+               const __grid_constant__ CUtensorMap map_y, int y_tma, int M, int N, int K, int NT, int nacc, int S,
+               int RW, int TM, const float* __restrict__ rowscale, const float* __restrict__ bias,
+               float* __restrict__ y, int acc) {
+  using CG = ColGeom<T>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int bhalf = (NT / 2) * 128;               // this CTA's NT/2 tokens x 64 K of fp16, 128-byte swizzled
+  const int bstage = 2 * bhalf;                   // one stage: two such boxes
+  const int wstage = kTmRows * CG::BB;            // the CTA's staged bytes of one 256-wide K column
+  uint8_t* sB = base;
+  float* sE = reinterpret_cast<float*>(sB + S * bstage);           // epilogue boxes: 2 per epilogue warp
+  uint8_t* sW = reinterpret_cast<uint8_t*>(sE + kPairEpiWarps * 2 * kTmEpiBox);
+  TmSmem* ctl = reinterpret_cast<TmSmem*>(sW + RW * wstage);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int TW = (N + 255) / 256;
+  const int NTILES = TM * TW * (NMAP == 1 ? 1 : pw.groups);
+  const int KB = K >> 8, nks = K / kTmStageK;
+  const uint32_t a_col0 = (uint32_t)(nacc * NT);  // first tensor-memory column of the A stages
+
+  if (tid == 0) {
+    for (int i = 0; i < RW; ++i) {
+      mbar_init(&ctl->wfull[i], 1);
+      mbar_init(&ctl->wempty[i], kTmDecodeWarps);
+    }
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&ctl->ofull[i], 2 + 2 * 8);       // rank 0 only: 2 producers + 8 decode warps per CTA
+      mbar_init(&ctl->oempty[i], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&ctl->acc_full[b], 1);
+      mbar_init(&ctl->acc_empty[b], 2 * kPairEpiWarps);
+    }
+    fence_mbar_init();
+  }
+  constexpr uint32_t kCols = 512;
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&ctl->tmem_base)),
+                 "r"(kCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();                             // barriers of both CTAs initialised, tensor memory allocated
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  if (NMAP > 1) grid_dep_wait();                  // the group row ranges come from the preceding kernel
+
+  if (warp == 0) {
+    // ---------------- TMA producer: activation tiles (B) ----------------
+    if (lane == 0) {
+      grid_dep_wait();
+      const uint32_t leader_ofull = mapa_shared(smem_u32(&ctl->ofull[0]), 0);
+      uint32_t s = 0, ph = 0;
+      for (int t = pair; t < NTILES; t += npairs) {
+        PairTile pt;
+        if (!tm_tile(pw, t, M, TM, TW, NT, pt)) continue;
+        const int bm = pt.am0 + (int)rank * (NT / 2);
+        for (int ks = 0; ks < nks; ++ks) {
+          pair_wait(&ctl->oempty[s], ph ^ 1);
+          uint8_t* dst = sB + s * bstage;
+          if (rank == 0) {
+            mbar_arrive_expect_tx(&ctl->ofull[s], (uint32_t)bstage);
+            tma_load_2d(dst, &map_b, ks * kTmStageK, bm, &ctl->ofull[s]);
+            tma_load_2d(dst + bhalf, &map_b, ks * kTmStageK + kBK, bm, &ctl->ofull[s]);
+          } else {
+            mbar_arrive_expect_tx_remote(leader_ofull + 8u * s, (uint32_t)bstage);
+            tma_load_2d_pair(dst, &map_b, ks * kTmStageK, bm, leader_ofull + 8u * s);
+            tma_load_2d_pair(dst + bhalf, &map_b, ks * kTmStageK + kBK, bm, leader_ofull + 8u * s);
+          }
+          if (++s == (uint32_t)S) { s = 0; ph ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---------------- MMA issuer ----------------
+      const uint32_t idesc = idesc_f16_f32_m256(NT);
+      const uint64_t b0 = smem_desc_sw128(sB);
+      const uint64_t bstep = (uint64_t)(bstage >> 4), bh = (uint64_t)(bhalf >> 4);
+      uint32_t s = 0, ph = 0, it = 0;
+      for (int t = pair; t < NTILES; t += npairs) {
+        PairTile pt;
+        if (!tm_tile(pw, t, M, TM, TW, NT, pt)) continue;
+        const uint32_t b = nacc == 2 ? (it & 1) : 0u, u = nacc == 2 ? (it >> 1) : it;
+        pair_wait(&ctl->acc_empty[b], (u & 1) ^ 1);
+        tc_fence_after();
+        const uint32_t d = tmem + b * (uint32_t)NT;
+        for (int ks = 0; ks < nks; ++ks) {
+          pair_wait(&ctl->ofull[s], ph);
+          tc_fence_after();
+          const uint64_t bs = b0 + s * bstep;
+          tc2_mma_stage128(d, tmem + a_col0 + s * 64u, (uint32_t)bs, (uint32_t)(bs >> 32), (uint32_t)bh, idesc,
+                           ks == 0 ? 1u : 0u);
+          tc2_commit_pair(&ctl->oempty[s]);      // both CTAs may refill the stage once these MMAs are done
+          if (++s == (uint32_t)S) { s = 0; ph ^= 1; }
+        }
+        tc2_commit_pair(&ctl->acc_full[b]);
+        ++it;
+      }
+    }
+  } else if (warp == 2) {
+    // ---------------- TMA producer: raw weight records ----------------
+    if (lane == 0) {
+      uint32_t rs = 0, rph = 0;
+      for (int t = pair; t < NTILES; t += npairs) {
+        PairTile pt;
+        if (!tm_tile(pw, t, M, TM, TW, NT, pt)) continue;
+        const CUtensorMap* wmap = &pw.map[NMAP == 1 ? 0 : pt.g];
+        const int wn = pt.col0 + (int)rank * kTmRows;
+        for (int kb = 0; kb < KB; ++kb) {
+          pair_wait(&ctl->wempty[rs], rph ^ 1);
+          mbar_arrive_expect_tx(&ctl->wfull[rs], (uint32_t)wstage);
+          const int wx = ((kb * CG::CB) & ~15) >> 1;   // 16-byte aligned start, in 16-bit elements
+          tma_load_2d(sW + rs * wstage, wmap, wx, wn, &ctl->wfull[rs]);
+          if (++rs == (uint32_t)RW) { rs = 0; rph ^= 1; }
+        }
+      }
+    }
+  } else if (warp >= 4 && warp < 4 + kTmDecodeWarps) {
+    // ---------------- decode into tensor memory ----------------
+    const int grp = (warp - 4) >> 3;              // stages 2c + grp of the columns c
+    const int hs = ((warp - 4) >> 2) & 1;         // 64-K half of the stage
+    const int j = 2 * grp + hs;                   // K step of each 256-wide column decoded by this warp
+    const int quarter = warp & 3;                 // the tensor-memory lanes this warp may access
+    const int row = quarter * 32 + lane;          // this thread's weight row in the CTA's 128
+    const uint32_t leader_ofull = mapa_shared(smem_u32(&ctl->ofull[0]), 0);
+    const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16) + a_col0 + (uint32_t)(hs * 32);
+    uint32_t s = (uint32_t)grp, ph = 0, rs = 0, rph = 0;   // this group's first stage is q = grp (< S)
+    for (int t = pair; t < NTILES; t += npairs) {
+      PairTile pt;
+      if (!tm_tile(pw, t, M, TM, TW, NT, pt)) continue;
+      for (int kb = 0; kb < KB; ++kb) {
+        pair_wait(&ctl->wfull[rs], rph);
+        const int mis = (kb * CG::CB) & 15;       // the column's offset in its staged box (0 for Q4_K)
+        const uint8_t* rec = sW + rs * wstage + row * CG::BB + mis;
+        pair_wait(&ctl->oempty[s], ph ^ 1);       // the MMAs that read these columns are done
+        tc_fence_after();
+        uint32_t hv[16];
+        item_regs<T>(rec, j, 0, hv);
+        tmem_st16(lane_addr + s * 64u, hv);
+        item_regs<T>(rec, j, 1, hv);
+        tmem_st16(lane_addr + s * 64u + 16u, hv);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (rank == 0)
+            mbar_arrive(&ctl->ofull[s]);
+          else
+            mbar_arrive_remote(leader_ofull + 8u * s);
+          mbar_arrive(&ctl->wempty[rs]);
+        }
+        s += 2;                                   // this group's stage of the next column
+        if (s >= (uint32_t)S) { s -= (uint32_t)S; ph ^= 1; }
+        if (++rs == (uint32_t)RW) { rs = 0; rph ^= 1; }
+      }
+    }
+  } else if (warp >= 4 + kTmDecodeWarps) {
+    // ---------------- epilogue ----------------
+    // Thread = output feature, tcgen05.ld column = token.  A 32-token chunk is
+    // scaled (row scale of each token, broadcast by shuffle), biased, written
+    // as a [token][feature] box into shared memory and sent to y by one bulk
+    // tensor store (or reduce-add when accumulating); the tensor map clips
+    // the box at M and N.  A chunk that crosses the end of its group's rows
+    // (grouped mode: the next rows belong to another group), or any chunk when
+    // y's row pitch is not a multiple of 16 bytes, is stored element-wise.
+    grid_dep_wait();                              // row scales come from the preceding kernel
+    const int quarter = warp & 3;
+    float* box0 = sE + quarter * 2 * kTmEpiBox;
+    uint32_t nb = 0;
+    const uint32_t leader_acc_empty = mapa_shared(smem_u32(&ctl->acc_empty[0]), 0);
+    uint32_t it = 0;
+    for (int t = pair; t < NTILES; t += npairs) {
+      PairTile pt;
+      if (!tm_tile(pw, t, M, TM, TW, NT, pt)) continue;
+      const uint32_t b = nacc == 2 ? (it & 1) : 0u, u = nacc == 2 ? (it >> 1) : it;
+      const int f0 = pt.col0 + (int)rank * kTmRows + quarter * 32;
+      const int f = f0 + lane;                    // this thread's output feature
+      const bool fok = f < N;
+      const int nch = NT / 32;
+      // row scales of the tile's tokens and the bias do not depend on the
+      // accumulator: read them before waiting for it
+      float rsv[8];
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        const int tok = pt.am0 + ch * 32 + lane;
+        rsv[ch] = (ch < nch && tok < pt.mhi) ? rowscale[tok] : 0.f;
+      }
+      const float bv = (bias && fok) ? bias[f] : 0.f;
+      pair_wait(&ctl->acc_full[b], u & 1);
+      tc_fence_after();
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        const int tok0 = pt.am0 + ch * 32;
+        if (ch >= nch || tok0 >= pt.mhi) break;
+        uint32_t v[32];
+        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + b * (uint32_t)NT + (uint32_t)(ch * 32), v);
+        tmem_ld_wait();
+        const float rs = rsv[ch];
+        if (y_tma && (NMAP == 1 || tok0 + 32 <= pt.mhi)) {
+          float* box = box0 + nb * kTmEpiBox;
+          if (lane == 0) bulk_wait_read1();       // the store issued from this box two chunks ago has read it
+          __syncwarp();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) box[c * 32 + lane] = __uint_as_float(v[c]) * __shfl_sync(~0u, rs, c) + bv;
+          fence_proxy_async_smem();               // generic-proxy writes -> visible to the bulk copy
+          __syncwarp();
+          if (lane == 0) {
+            if (acc)
+              tma_reduce_add_2d(&map_y, box, f0, tok0);
+            else
+              tma_store_2d(&map_y, box, f0, tok0);
+            bulk_commit();
+          }
+          nb ^= 1;
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const float o = __uint_as_float(v[c]) * __shfl_sync(~0u, rs, c) + bv;
+            const int tok = tok0 + c;
+            if (tok < pt.mhi && fok) {
+              float* yp = y + (int64_t)tok * N + f;
+              if (acc)
+                *yp += o;
+              else
+                *yp = o;
+            }
+          }
+        }
+      }
+      tc_fence_before();                          // this warp's tensor-memory reads are complete
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0)
+          mbar_arrive(&ctl->acc_empty[b]);
+        else
+          mbar_arrive_remote(leader_acc_empty + 8u * b);
+      }
+      ++it;
+    }
+    if (lane == 0) bulk_wait_all();               // every store has completed before the CTA exits
+    __syncwarp();
+  }
+  tc_fence_before();
+  cluster_sync_all();                             // no arrival or MMA read of the peer's memory is outstanding
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -1075,12 +1637,12 @@ TileCfg choose_tile(int64_t M, int64_t N, int64_t K, int sms) {
 }  // namespace
 
 namespace {
-int encode_a16(CUtensorMap* map, const __half* a16, int64_t rows, int64_t k) {
+int encode_a16(CUtensorMap* map, const __half* a16, int64_t rows, int64_t k, int box_rows = 128) {
   EncodeTiledFn encode = get_encode();
   if (!encode) return xm_set_error(XM_ERR_CUDA, "qgemm: cuTensorMapEncodeTiled unavailable");
   const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)k * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kBK, 128};
+  const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
   const cuuint32_t es[2] = {1, 1};
   CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(a16), dims, strides, box, es,
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1142,9 +1704,10 @@ const void* pair_kernel() {
   return reinterpret_cast<const void*>(k_qgemm_pair<T, kPairDW, NMAP>);
 }
 
-// How many CTA pairs of a kernel and shared-memory size can be resident at
-// once (0 if the device cannot launch it); cached per device, kernel and size.
-int pair_capacity(const void* fn, const PairCfg& cfg) {
+// How many CTA pairs of a kernel, block size and shared-memory size can be
+// resident at once (0 if the device cannot launch it); cached per device,
+// kernel and size.
+int cluster_capacity(const void* fn, int threads, int smem) {
   struct Key {
     int dev;
     const void* fn;
@@ -1159,14 +1722,14 @@ int pair_capacity(const void* fn, const PairCfg& cfg) {
   {
     std::lock_guard<std::mutex> lock(mu);
     for (int i = 0; i < used; ++i)
-      if (keys[i].dev == dev && keys[i].fn == fn && keys[i].smem == cfg.smem) return vals[i];
+      if (keys[i].dev == dev && keys[i].fn == fn && keys[i].smem == smem) return vals[i];
   }
   int n = 0;
-  if (cfg.S >= 3 && cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, cfg.smem) == cudaSuccess) {
+  if (smem > 0 && cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess) {
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3(2);
-    lc.blockDim = dim3(pair_threads(kPairDW));
-    lc.dynamicSmemBytes = cfg.smem;
+    lc.blockDim = dim3(threads);
+    lc.dynamicSmemBytes = smem;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
@@ -1179,11 +1742,15 @@ int pair_capacity(const void* fn, const PairCfg& cfg) {
   cudaGetLastError();
   std::lock_guard<std::mutex> lock(mu);
   if (used < 256) {
-    keys[used] = Key{dev, fn, cfg.smem};
+    keys[used] = Key{dev, fn, smem};
     vals[used] = n;
     ++used;
   }
   return n;
+}
+
+int pair_capacity(const void* fn, const PairCfg& cfg) {
+  return cfg.S >= 3 ? cluster_capacity(fn, pair_threads(kPairDW), cfg.smem) : 0;
 }
 
 // Tile shape for `mtiles` 256-row tiles of output width n: BN (multiple of 32,
@@ -1313,6 +1880,161 @@ int launch_pair_grouped(const CUtensorMap& map_a, const uint8_t* const* h_w, con
   return launch_pair<T, kMaxGroups>(map_a, pw, P, n, k, tm, cfg, pairs, rowscale, nullptr, y, 0, st);
 }
 
+// ---- tensor-memory-A kernel ----
+struct TmCfg {
+  int NT, nacc, S, RW, smem;
+};
+
+int tm_smem_bytes(int NT, int S, int RW, int BB) {
+  return 1024 + S * (NT / 2) * 256 + kPairEpiWarps * 2 * kTmEpiBox * 4 + RW * kTmRows * BB + (int)sizeof(TmSmem);
+}
+
+// fp32 output [rows][n] as a tensor map with 32 x 32 boxes; false when the
+// row pitch is not a multiple of 16 bytes (element-wise stores then).
+bool encode_y_map(CUtensorMap* map, const float* y, int64_t rows, int64_t n) {
+  if ((n * 4) % 16 || ((uintptr_t)y & 15)) return false;
+  EncodeTiledFn encode = get_encode();
+  if (!encode) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)n * 4};
+  const cuuint32_t box[2] = {32, 32};
+  const cuuint32_t es[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(y), dims, strides, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Token-tile options: NT a multiple of 32 (<= 256); two accumulators where
+// they fit beside 4 A stages (so the epilogue of one tile overlaps the next
+// tile's main loop), then as many A stages (<= 6) as tensor and shared memory
+// hold.  S = 0 if fewer than 3 stages fit.
+TmCfg tm_stages(int NT, int BB) {
+  const int nacc = 2 * NT + 4 * 64 <= 512 ? 2 : 1;
+  int S = std::min(kTmMaxStages, (512 - nacc * NT) / 64);
+  while (S >= 3 && tm_smem_bytes(NT, S, kPairRaw, BB) > 227 * 1024) --S;
+  if (S < 3) S = 0;
+  return {NT, nacc, S, kPairRaw, tm_smem_bytes(NT, S, kPairRaw, BB)};
+}
+
+template <int T, int NMAP>
+const void* tm_kernel() {
+  return reinterpret_cast<const void*>(k_qgemm_tm<T, NMAP>);
+}
+
+// Token tile for m rows (per group) and n output features: estimated clocks
+// per pair = rounds x (main loop + the epilogues that do not overlap it).  A
+// 128-K stage costs the larger of its MMA time (4 NT clocks) and the issuing
+// thread's cost (8 MMA issues and a barrier wait beside 16 decode warps,
+// ~1120 clocks measured); the epilogue ~1400 + 20 NT clocks.
+TmCfg choose_tm(int64_t m, int64_t groups, int64_t n, int64_t k, int pairs, int BB) {
+  TmCfg best{0, 0, 0, 0, 0};
+  double best_t = 1e30;
+  const double nks = (double)(k / kTmStageK);
+  const int64_t tw = (n + 255) / 256;
+  for (int nt = 256; nt >= 32; nt -= 32) {
+    if (nt > 32 && nt - 32 >= m) continue;      // a smaller tile already holds every row
+    const TmCfg c = tm_stages(nt, BB);
+    if (c.S < 3) continue;
+    const int64_t tiles = groups * tw * ((m + nt - 1) / nt);
+    const double rounds = (double)((tiles + pairs - 1) / pairs);
+    const double main_clk = nks * std::max(1120.0, 4.0 * nt + 90.0);
+    const double epi_clk = 1400.0 + 20.0 * nt;
+    const double t = rounds * main_clk + (c.nacc == 1 ? rounds : 1.0) * epi_clk;
+    if (t < best_t) {
+      best_t = t;
+      best = c;
+    }
+  }
+  return best;
+}
+
+template <int T, int NMAP>
+int launch_tm(const CUtensorMap& map_b, const PairW<NMAP>& pw, int64_t m, int64_t n, int64_t k, int tm,
+              const TmCfg& cfg, int pairs, const float* rowscale, const float* bias, float* y, int acc,
+              cudaStream_t st) {
+  const void* fn = tm_kernel<T, NMAP>();
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, cfg.smem);
+  if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemm: smem attribute: %s", cudaGetErrorString(e));
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3((unsigned)(2 * pairs));
+  lc.blockDim = dim3(kTmThreads);
+  lc.dynamicSmemBytes = cfg.smem;
+  lc.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 2;
+  CUtensorMap map_y;
+  memset(&map_y, 0, sizeof(map_y));
+  const int y_tma = encode_y_map(&map_y, y, m, n) ? 1 : 0;
+  e = cudaLaunchKernelEx(&lc, k_qgemm_tm<T, NMAP>, map_b, pw, map_y, y_tma, (int)m, (int)n, (int)k, cfg.NT,
+                         cfg.nacc, cfg.S, cfg.RW, tm, rowscale, bias, y, acc);
+  if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemm tm launch: %s", cudaGetErrorString(e));
+  return xm_check_launch("qgemm tm");
+}
+
+// Dense GEMM on the tensor-memory-A kernel; 1 (nothing launched) if the
+// device cannot hold it.
+template <int T>
+int launch_tm_gemm(const __half* a16, const uint8_t* w, int64_t m, int64_t n, int64_t k, const float* rowscale,
+                   const float* bias, float* y, int acc, cudaStream_t st) {
+  constexpr int BB = ColGeom<T>::BB;
+  const void* fn = tm_kernel<T, 1>();
+  const TmCfg probe = tm_stages(128, BB);
+  const int cap = cluster_capacity(fn, kTmThreads, probe.smem);
+  if (cap < 1) return 1;
+  const TmCfg cfg = choose_tm(m, 1, n, k, cap, BB);
+  if (cfg.S < 3) return 1;
+  const int cap_cfg = cluster_capacity(fn, kTmThreads, cfg.smem);
+  if (cap_cfg < 1) return 1;
+  CUtensorMap map_b;
+  int rc = encode_a16(&map_b, a16, m, k, cfg.NT / 2);
+  if (rc) return rc;
+  PairW<1> pw{};
+  rc = encode_w_records<T>(&pw.map[0], w, n, k, kTmRows);
+  if (rc) return rc;
+  pw.groups = 1;
+  const int64_t tm = (m + cfg.NT - 1) / cfg.NT;
+  const int64_t tiles = tm * ((n + 255) / 256);
+  const int pairs = (int)std::min<int64_t>(tiles, cap_cfg);
+  return launch_tm<T, 1>(map_b, pw, m, n, k, (int)tm, cfg, pairs, rowscale, bias, y, acc, st);
+}
+
+template <int T>
+int launch_tm_grouped(const __half* a16, const uint8_t* const* h_w, const int* d_cnt, const int* d_off, int G,
+                      int64_t P, int64_t n, int64_t k, int64_t max_rows, int64_t expect_rows, const float* rowscale,
+                      float* y, cudaStream_t st) {
+  constexpr int BB = ColGeom<T>::BB;
+  const void* fn = tm_kernel<T, kMaxGroups>();
+  const TmCfg probe = tm_stages(128, BB);
+  const int cap = cluster_capacity(fn, kTmThreads, probe.smem);
+  if (cap < 1) return 1;
+  const TmCfg cfg = choose_tm(expect_rows, G, n, k, cap, BB);
+  if (cfg.S < 3) return 1;
+  const int cap_cfg = cluster_capacity(fn, kTmThreads, cfg.smem);
+  if (cap_cfg < 1) return 1;
+  CUtensorMap map_b;
+  int rc = encode_a16(&map_b, a16, P, k, cfg.NT / 2);
+  if (rc) return rc;
+  PairW<kMaxGroups> pw{};
+  for (int g = 0; g < G; ++g) {
+    rc = encode_w_records<T>(&pw.map[g], h_w[g], n, k, kTmRows);
+    if (rc) return rc;
+  }
+  pw.cnt = d_cnt;
+  pw.off = d_off;
+  pw.groups = G;
+  const int tm = (int)((max_rows + cfg.NT - 1) / cfg.NT);
+  const int64_t tiles = (int64_t)G * tm * ((n + 255) / 256);
+  const int pairs = (int)std::min<int64_t>(tiles, cap_cfg);
+  return launch_tm<T, kMaxGroups>(map_b, pw, P, n, k, tm, cfg, pairs, rowscale, nullptr, y, 0, st);
+}
+
 // Runtime type id -> the launchers above (dispatch_quant calls operator()<T>).
 struct PairDense {
   const CUtensorMap* map_a;
@@ -1322,10 +2044,13 @@ struct PairDense {
   float* y;
   int acc;
   cudaStream_t st;
+  const __half* a16;
   int rc = 1;
   template <int T>
   void operator()() {
-    rc = launch_pair_gemm<T>(*map_a, w, m, n, k, rowscale, bias, y, acc, st);
+    // tensor-memory-A kernel; the CTA-pair kernel where the device cannot hold it
+    rc = launch_tm_gemm<T>(a16, w, m, n, k, rowscale, bias, y, acc, st);
+    if (rc == 1) rc = launch_pair_gemm<T>(*map_a, w, m, n, k, rowscale, bias, y, acc, st);
   }
 };
 
@@ -1338,10 +2063,13 @@ struct PairGrouped {
   const float* rowscale;
   float* y;
   cudaStream_t st;
+  const __half* a16;
   int rc = 1;
   template <int T>
   void operator()() {
-    rc = launch_pair_grouped<T>(*map_a, h_w, cnt, off, G, P, n, k, max_rows, expect_rows, rowscale, y, st);
+    rc = launch_tm_grouped<T>(a16, h_w, cnt, off, G, P, n, k, max_rows, expect_rows, rowscale, y, st);
+    if (rc == 1)
+      rc = launch_pair_grouped<T>(*map_a, h_w, cnt, off, G, P, n, k, max_rows, expect_rows, rowscale, y, st);
   }
 };
 
@@ -1379,7 +2107,7 @@ int qgemm_grouped(int qtype, const __half* a16, const float* rowscale, int64_t P
   CUtensorMap map_a;
   int rc = encode_a16(&map_a, a16, P, K);
   if (rc) return rc;
-  PairGrouped pg{&map_a, h_w, d_cnt, d_off, G, P, N, K, max_rows, expect_rows, rowscale, y, st};
+  PairGrouped pg{&map_a, h_w, d_cnt, d_off, G, P, N, K, max_rows, expect_rows, rowscale, y, st, a16};
   dispatch_quant(qtype, pg);
   if (pg.rc != 1) return pg.rc;
   if (qtype != T_Q4_K)
@@ -1466,7 +2194,7 @@ extern "C" int xm_qgemm_ex(int qtype, const void* d_w, int64_t w_bytes, int64_t 
   CUtensorMap map_a;
   rc = encode_a16(&map_a, x16, m, k);
   if (rc) return rc;
-  PairDense pd{&map_a, (const uint8_t*)d_w, m, n, k, rowscale, d_bias, d_y, accumulate ? 1 : 0, st};
+  PairDense pd{&map_a, (const uint8_t*)d_w, m, n, k, rowscale, d_bias, d_y, accumulate ? 1 : 0, st, x16};
   dispatch_quant(qtype, pd);
   if (pd.rc != 1) return pd.rc;
   if (qtype != T_Q4_K)
