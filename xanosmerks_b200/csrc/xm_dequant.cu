@@ -6,7 +6,7 @@
 // memory would issue many narrow loads), then every thread decodes groups of
 // 8 consecutive elements and writes them with one 16-byte (fp16) or two
 // 16-byte (fp32) stores, fully coalesced.
-#include "xm_qtypes.cuh"
+#include "xm_decode.cuh"
 
 namespace {
 
@@ -59,6 +59,36 @@ __global__ void __launch_bounds__(kThreads) k_dequant(const uint8_t* __restrict_
   }
 }
 
+// fp16 output, 16-byte-aligned input whose element count is a multiple of
+// 256: one thread per 32-element item (a quarter-record of a 256-element
+// super-block, or one of eight 32-element records), decoded word-wise
+// (xm_decode) into 16 fp16 pairs and written with four 16-byte stores.  A CTA
+// stages 32 consecutive 256-element columns (8192 elements).
+constexpr int kItemCols = 32;
+template <int T>
+struct ItemCfg {
+  static constexpr int CB = QT<T>::REC * (256 / QT<T>::QK);   // bytes of one 256-element column
+  static constexpr int SMEM = kItemCols * CB + 32;            // + slack for the 16-byte over-read
+};
+
+template <int T>
+__global__ void __launch_bounds__(kThreads) k_dequant_items(const uint8_t* __restrict__ raw, int64_t n_cols,
+                                                            __half* __restrict__ out) {
+  constexpr int CB = ItemCfg<T>::CB;
+  __shared__ __align__(16) uint8_t sm[ItemCfg<T>::SMEM];
+  const int64_t c0 = (int64_t)blockIdx.x * kItemCols;
+  const int nc = (int)min((int64_t)kItemCols, n_cols - c0);
+  stage_bytes(sm, raw + c0 * CB, nc * CB, threadIdx.x, kThreads);   // 16-byte aligned source: no offset
+  __syncthreads();
+  const int col = threadIdx.x >> 3, it = threadIdx.x & 7;
+  if (col >= nc) return;
+  uint32_t hv[16];
+  xm_decode::item_regs<T>(sm + col * CB, it >> 1, it & 1, hv);
+  uint4* o = reinterpret_cast<uint4*>(out + (c0 + col) * 256 + 32 * it);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) o[q] = make_uint4(hv[4 * q], hv[4 * q + 1], hv[4 * q + 2], hv[4 * q + 3]);
+}
+
 // Plain (non-block) types, one element per thread-iteration.
 template <typename OutT>
 XM_DEV void put(OutT* o, int64_t i, float v);
@@ -98,6 +128,13 @@ struct LaunchDequant {
   cudaStream_t stream;
   template <int T>
   void operator()() {
+    if (out_dtype == XM_DT_F16 && ((uintptr_t)raw & 15) == 0 && (n_blocks * QT<T>::QK) % 256 == 0) {
+      const int64_t n_cols = n_blocks * QT<T>::QK / 256;
+      const int64_t grid = (n_cols + kItemCols - 1) / kItemCols;
+      if (grid == 0) return;
+      k_dequant_items<T><<<(unsigned)grid, kThreads, 0, stream>>>(raw, n_cols, (__half*)out);
+      return;
+    }
     constexpr int BPC = DequantCfg<T>::BPC;
     const int64_t grid = (n_blocks + BPC - 1) / BPC;
     if (grid == 0) return;
