@@ -187,6 +187,16 @@ XM_DEV float block_sum(float v, float* red) {
   return r;
 }
 
+// Expert activations (moe.py / primitives.py): silu x / (1 + exp(-x)), gelu
+// (tanh form) 0.5 x (1 + tanh(0.7978845608 (x + 0.044715 x^3))), relu
+// max(x, 0), identity.  `act` is an XM_ACT_* id.
+XM_DEV float xm_act(int act, float x) {
+  if (act == XM_ACT_SILU) return x / (1.0f + expf(-x));
+  if (act == XM_ACT_GELU) return 0.5f * x * (1.0f + tanhf(0.7978845608f * (x + 0.044715f * x * x * x)));
+  if (act == XM_ACT_RELU) return fmaxf(x, 0.0f);
+  return x;
+}
+
 // The power-of-two exponent s with amax / 2^s in [2^14, 2^15) (0 for zero or non-finite rows).
 XM_DEV int fp16_row_shift(float amax) {
   int s = 0;

@@ -13,6 +13,12 @@
 int qgemm_grouped(int qtype, const __half* a16, const float* rowscale, int64_t P, int64_t K, int64_t N,
                   const uint8_t* const* h_w, const int* d_cnt, const int* d_off, int G, int64_t max_rows,
                   int64_t expect_rows, float* y, cudaStream_t st);
+// Gate/up experts fused: y = act(a W1^T) * (a W3^T) per group (XM_ACT_* act),
+// fp32 out.  Returns 1 (nothing launched) when the device cannot hold the
+// kernel, so the caller can run the two projections separately.
+int qgemm_grouped_gate_up(int qtype, int act, const __half* a16, const float* rowscale, int64_t P, int64_t K,
+                          int64_t N, const uint8_t* const* h_w1, const uint8_t* const* h_w3, const int* d_cnt,
+                          const int* d_off, int G, int64_t max_rows, int64_t expect_rows, float* y, cudaStream_t st);
 // Whether the tensor-core GEMM takes weights of this type with rows of k
 // elements (k a multiple of 256 and a row a multiple of 16 bytes).
 bool qgemm_type_supported(int qtype, int64_t k);

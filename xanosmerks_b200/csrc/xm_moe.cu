@@ -187,10 +187,7 @@ __global__ void __launch_bounds__(256) k_moe_gather(const XT* __restrict__ x, co
 // 0.044715 x^3))), relu max(x, 0), identity.
 template <int ACT>
 XM_DEV float expert_act(float x) {
-  if constexpr (ACT == XM_ACT_SILU) return x / (1.0f + expf(-x));
-  else if constexpr (ACT == XM_ACT_GELU) return 0.5f * x * (1.0f + tanhf(0.7978845608f * (x + 0.044715f * x * x * x)));
-  else if constexpr (ACT == XM_ACT_RELU) return fmaxf(x, 0.0f);
-  else return x;
+  return xm_act(ACT, x);
 }
 
 template <int ACT>
@@ -210,6 +207,46 @@ __global__ void __launch_bounds__(kPrepThreads) k_swiglu_prep(const float* __res
         for (int i = 0; i < 4; ++i) v[i] = expert_act<ACT>(v[i]) * uu[i];
       },
       F, h16 + (int64_t)p * F, hscale + p, red);
+}
+
+// fp32 rows (P x F) -> fp16 with a power-of-two row scale, one block per row,
+// the row held in shared memory between the max and the conversion (one
+// read of the row).  Dynamic shared memory: F floats.
+__global__ void __launch_bounds__(kPrepThreads) k_rows_fp16(const float* __restrict__ h, int F, __half* __restrict__ h16,
+                                                            float* __restrict__ hscale) {
+  extern __shared__ float4 rowc[];
+  __shared__ float red[32];
+  const int p = blockIdx.x;
+  const float4* hr = reinterpret_cast<const float4*>(h + (int64_t)p * F);
+  const int F4 = F >> 2;
+  float amax = 0.f;
+  int k = threadIdx.x;
+  for (; k + 3 * kPrepThreads < F4; k += 4 * kPrepThreads) {   // four independent loads in flight per thread
+    float4 v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = __ldcs(hr + k + i * kPrepThreads);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      rowc[k + i * kPrepThreads] = v[i];
+      amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+    }
+  }
+  for (; k < F4; k += kPrepThreads) {
+    const float4 v = __ldcs(hr + k);
+    rowc[k] = v;
+    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  }
+  amax = block_max(amax, red);                    // (its barrier also orders the row cache)
+  const int s = fp16_row_shift(amax);
+  const float inv = ldexpf(1.0f, -s);
+  __half* o = h16 + (int64_t)p * F;
+  for (k = threadIdx.x; k < F4; k += kPrepThreads) {
+    const float4 v = rowc[k];
+    const __half2 a = __floats2half2_rn(v.x * inv, v.y * inv), b = __floats2half2_rn(v.z * inv, v.w * inv);
+    *reinterpret_cast<uint2*>(o + 4 * k) = make_uint2(*reinterpret_cast<const uint32_t*>(&a),
+                                                      *reinterpret_cast<const uint32_t*>(&b));
+  }
+  if (threadIdx.x == 0) hscale[p] = ldexpf(1.0f, s);
 }
 
 // out[t] = sum over the token's k expert rows, ascending expert order, of
@@ -343,6 +380,26 @@ int run_experts(int qtype, int act, const __half* a16, const float* ascale, int6
                 float* u, __half* h16, float* hscale, float* d, cudaStream_t st) {
   const int64_t expect = std::max<int64_t>(1, P / G);
   int rc;
+  // w1 and w3 in one pass with act(gate) * up in the epilogue (g holds the
+  // product), then one read of it for the fp16 conversion
+  const int64_t rows_smem = F * (int64_t)sizeof(float);
+  if (rows_smem <= 200 * 1024) {
+    rc = qgemm_grouped_gate_up(qtype, act, a16, ascale, P, H, F, tab, tab + G, cnt, off, G, max_rows, expect, g, st);
+    if (rc != 1) {
+      if (rc) return rc;
+      static bool attr_done[64] = {};
+      int dev = 0;
+      cudaGetDevice(&dev);
+      if (rows_smem > 48 * 1024 && (dev < 0 || dev >= 64 || !attr_done[dev])) {
+        cudaError_t e = cudaFuncSetAttribute(k_rows_fp16, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "moe: smem attribute: %s", cudaGetErrorString(e));
+        if (dev >= 0 && dev < 64) attr_done[dev] = true;
+      }
+      k_rows_fp16<<<(unsigned)P, kPrepThreads, (size_t)rows_smem, st>>>(g, (int)F, h16, hscale);
+      if ((rc = xm_check_launch("moe rows fp16"))) return rc;
+      return qgemm_grouped(qtype, h16, hscale, P, F, H, tab + 2 * G, cnt, off, G, max_rows, expect, d, st);
+    }
+  }
   if ((rc = qgemm_grouped(qtype, a16, ascale, P, H, F, tab, cnt, off, G, max_rows, expect, g, st))) return rc;
   if ((rc = qgemm_grouped(qtype, a16, ascale, P, H, F, tab + G, cnt, off, G, max_rows, expect, u, st))) return rc;
   const unsigned pgrid = (unsigned)P;     // one block per row

@@ -1070,6 +1070,7 @@ struct TmSmem {
   uint32_t tmem_base;
 };
 
+
 XM_DEV void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
@@ -1094,15 +1095,6 @@ XM_DEV void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int c0, i
 XM_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 XM_DEV void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 XM_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-
-// D[tmem] (+)= A[tmem] * B[smem descriptor], both CTAs of the pair
-XM_DEV void tc2_mma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n}"
-      ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 
 // The 8 MMAs of one 128-K stage (K = 16 each) in one instruction block, so
 // that the issuing thread, which shares its scheduler with decode warps, runs
@@ -1141,15 +1133,44 @@ XM_DEV void tc2_mma_stage128(uint32_t d, uint32_t a, uint32_t blo, uint32_t bhi,
       : "memory");
 }
 
+// Gate/up epilogue, one warp pair (gate warp: lanes = w1 rows, up warp: the
+// same features' w3 rows) and one 32-token chunk: each warp evaluates
+// act(gate) * up for 16 tokens, the gate warp for tokens 0-15 (its own gate
+// values, the up values from `xu`), the up warp for 16-31 (the gate values
+// from `xg`, its own up values); o[c - c0] = the result for token c.  Only the
+// epilogue warps evaluate the activation, beside busy decode warps, so SiLU
+// uses the fast exponential and division intrinsics (a few ulp from x / (1 +
+// exp(-x)) in fp32; 0 for x -> -inf).
+template <int ACT>
+XM_DEV float gate_act(float x) {
+  if constexpr (ACT == XM_ACT_SILU) return __fdividef(x, 1.0f + __expf(-x));
+  else return xm_act(ACT, x);
+}
+template <int ACT>
+XM_DEV void gate_up_half(const uint32_t (&v)[32], float rs, bool gate, const float* xg, const float* xu,
+                         float (&o)[16]) {
+  if (gate) {
+#pragma unroll
+    for (int c = 0; c < 16; ++c)
+      o[c] = gate_act<ACT>(__uint_as_float(v[c]) * __shfl_sync(~0u, rs, c)) * xu[c * 32];
+  } else {
+#pragma unroll
+    for (int c = 0; c < 16; ++c)
+      o[c] = gate_act<ACT>(xg[c * 32]) * (__uint_as_float(v[16 + c]) * __shfl_sync(~0u, rs, 16 + c));
+  }
+}
+XM_DEV void named_bar(int id, int threads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory"); }
+
 // Tile t of the tensor-memory-A kernel: token tile (fastest, so that the
-// pairs that run together share a weight tile in L2) and 256-row weight tile.
+// pairs that run together share a weight tile in L2) and weight tile of W
+// output features (256; 128 in gate/up mode).
 template <int NMAP>
-XM_DEV bool tm_tile(const PairW<NMAP>& pw, int t, int M, int TM, int TW, int NT, PairTile& pt) {
+XM_DEV bool tm_tile(const PairW<NMAP>& pw, int t, int M, int TM, int TW, int NT, int W, PairTile& pt) {
   if (NMAP == 1) {
     pt.g = 0;
     pt.am0 = (t % TM) * NT;
     pt.mhi = M;
-    pt.col0 = (t / TM) * 256;
+    pt.col0 = (t / TM) * W;
     return true;
   }
   const int wt = t % TW, r = t / TW;
@@ -1158,17 +1179,23 @@ XM_DEV bool tm_tile(const PairW<NMAP>& pw, int t, int M, int TM, int TW, int NT,
   pt.g = g;
   pt.am0 = lo + mt * NT;
   pt.mhi = lo + cnt;
-  pt.col0 = wt * 256;
+  pt.col0 = wt * W;
   return mt * NT < cnt;
 }
 
-template <int T, int NMAP>
+// GU (gate/up mode, grouped): each CTA's 128 MMA rows are 64 rows of w1 (map
+// pw; tensor-memory lanes 0-63) and the same 64 rows of w3 (map pw3; lanes
+// 64-127), so the epilogue warps of lane quarters q and q + 2 hold the gate
+// and up accumulators of the same features and combine them through shared
+// memory: y = act(gate) * up, 128 features per CTA pair.
+template <int T, int NMAP, bool GU>
 __global__ void __launch_bounds__(kTmThreads, 1)
     k_qgemm_tm(const __grid_constant__ CUtensorMap map_b, const __grid_constant__ PairW<NMAP> pw,
-               const __grid_constant__ CUtensorMap map_y, int y_tma, int M, int N, int K, int NT, int nacc, int S,
-               int RW, int TM, const float* __restrict__ rowscale, const float* __restrict__ bias,
-               float* __restrict__ y, int acc) {
+               const __grid_constant__ PairW<NMAP> pw3, const __grid_constant__ CUtensorMap map_y, int y_tma, int M,
+               int N, int K, int NT, int nacc, int S, int RW, int TM, const float* __restrict__ rowscale,
+               const float* __restrict__ bias, float* __restrict__ y, int acc, int act) {
   using CG = ColGeom<T>;
+  constexpr int TWID = GU ? kTmRows : 2 * kTmRows;   // output features per tile
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int bhalf = (NT / 2) * 128;               // this CTA's NT/2 tokens x 64 K of fp16, 128-byte swizzled
@@ -1176,13 +1203,14 @@ __global__ void __launch_bounds__(kTmThreads, 1)
   const int wstage = kTmRows * CG::BB;            // the CTA's staged bytes of one 256-wide K column
   uint8_t* sB = base;
   float* sE = reinterpret_cast<float*>(sB + S * bstage);           // epilogue boxes: 2 per epilogue warp
-  uint8_t* sW = reinterpret_cast<uint8_t*>(sE + kPairEpiWarps * 2 * kTmEpiBox);
+  float* sU = sE + kPairEpiWarps * 2 * kTmEpiBox;                   // gate/up: per warp pair 2 x [16][32]
+  uint8_t* sW = reinterpret_cast<uint8_t*>(sU + (GU ? 2 * kTmEpiBox : 0));
   TmSmem* ctl = reinterpret_cast<TmSmem*>(sW + RW * wstage);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t rank = cluster_ctarank();
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  const int TW = (N + 255) / 256;
+  const int TW = (N + TWID - 1) / TWID;
   const int NTILES = TM * TW * (NMAP == 1 ? 1 : pw.groups);
   const int KB = K >> 8, nks = K / kTmStageK;
   const uint32_t a_col0 = (uint32_t)(nacc * NT);  // first tensor-memory column of the A stages
@@ -1223,7 +1251,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
       uint32_t s = 0, ph = 0;
       for (int t = pair; t < NTILES; t += npairs) {
         PairTile pt;
-        if (!tm_tile(pw, t, M, TM, TW, NT, pt)) continue;
+        if (!tm_tile(pw, t, M, TM, TW, NT, TWID, pt)) continue;
         const int bm = pt.am0 + (int)rank * (NT / 2);
         for (int ks = 0; ks < nks; ++ks) {
           pair_wait(&ctl->oempty[s], ph ^ 1);
@@ -1250,7 +1278,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
       uint32_t s = 0, ph = 0, it = 0;
       for (int t = pair; t < NTILES; t += npairs) {
         PairTile pt;
-        if (!tm_tile(pw, t, M, TM, TW, NT, pt)) continue;
+        if (!tm_tile(pw, t, M, TM, TW, NT, TWID, pt)) continue;
         const uint32_t b = nacc == 2 ? (it & 1) : 0u, u = nacc == 2 ? (it >> 1) : it;
         pair_wait(&ctl->acc_empty[b], (u & 1) ^ 1);
         tc_fence_after();
@@ -1274,14 +1302,16 @@ __global__ void __launch_bounds__(kTmThreads, 1)
       uint32_t rs = 0, rph = 0;
       for (int t = pair; t < NTILES; t += npairs) {
         PairTile pt;
-        if (!tm_tile(pw, t, M, TM, TW, NT, pt)) continue;
+        if (!tm_tile(pw, t, M, TM, TW, NT, TWID, pt)) continue;
         const CUtensorMap* wmap = &pw.map[NMAP == 1 ? 0 : pt.g];
-        const int wn = pt.col0 + (int)rank * kTmRows;
+        const CUtensorMap* wmap3 = &pw3.map[NMAP == 1 ? 0 : pt.g];
+        const int wn = pt.col0 + (GU ? (int)rank * (kTmRows / 2) : (int)rank * kTmRows);
         for (int kb = 0; kb < KB; ++kb) {
           pair_wait(&ctl->wempty[rs], rph ^ 1);
           mbar_arrive_expect_tx(&ctl->wfull[rs], (uint32_t)wstage);
           const int wx = ((kb * CG::CB) & ~15) >> 1;   // 16-byte aligned start, in 16-bit elements
           tma_load_2d(sW + rs * wstage, wmap, wx, wn, &ctl->wfull[rs]);
+          if (GU) tma_load_2d(sW + rs * wstage + (kTmRows / 2) * CG::BB, wmap3, wx, wn, &ctl->wfull[rs]);
           if (++rs == (uint32_t)RW) { rs = 0; rph ^= 1; }
         }
       }
@@ -1298,7 +1328,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     uint32_t s = (uint32_t)grp, ph = 0, rs = 0, rph = 0;   // this group's first stage is q = grp (< S)
     for (int t = pair; t < NTILES; t += npairs) {
       PairTile pt;
-      if (!tm_tile(pw, t, M, TM, TW, NT, pt)) continue;
+      if (!tm_tile(pw, t, M, TM, TW, NT, TWID, pt)) continue;
       for (int kb = 0; kb < KB; ++kb) {
         pair_wait(&ctl->wfull[rs], rph);
         const int mis = (kb * CG::CB) & 15;       // the column's offset in its staged box (0 for Q4_K)
@@ -1342,9 +1372,9 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     uint32_t it = 0;
     for (int t = pair; t < NTILES; t += npairs) {
       PairTile pt;
-      if (!tm_tile(pw, t, M, TM, TW, NT, pt)) continue;
+      if (!tm_tile(pw, t, M, TM, TW, NT, TWID, pt)) continue;
       const uint32_t b = nacc == 2 ? (it & 1) : 0u, u = nacc == 2 ? (it >> 1) : it;
-      const int f0 = pt.col0 + (int)rank * kTmRows + quarter * 32;
+      const int f0 = pt.col0 + (GU ? (int)rank * (kTmRows / 2) + (quarter & 1) * 32 : (int)rank * kTmRows + quarter * 32);
       const int f = f0 + lane;                    // this thread's output feature
       const bool fok = f < N;
       const int nch = NT / 32;
@@ -1367,12 +1397,59 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + b * (uint32_t)NT + (uint32_t)(ch * 32), v);
         tmem_ld_wait();
         const float rs = rsv[ch];
+        if constexpr (GU) {
+          const int wp = quarter & 1;            // warp pair: gate warp wp, up warp wp + 2
+          const bool gate = quarter < 2;
+          float* xg = sU + wp * kTmEpiBox;       // [16][32]: the gate values of tokens 16-31
+          float* xu = xg + kTmEpiBox / 2;        // [16][32]: the up values of tokens 0-15
+          if (gate) {
+#pragma unroll
+            for (int c = 16; c < 32; ++c) xg[(c - 16) * 32 + lane] = __uint_as_float(v[c]) * __shfl_sync(~0u, rs, c);
+          } else {
+#pragma unroll
+            for (int c = 0; c < 16; ++c) xu[c * 32 + lane] = __uint_as_float(v[c]) * __shfl_sync(~0u, rs, c);
+          }
+          const bool tma_ok = y_tma && (NMAP == 1 || tok0 + 32 <= pt.mhi);
+          float* box = sE + wp * 2 * kTmEpiBox + nb * kTmEpiBox;   // the pair's output box
+          if (tma_ok && gate && lane == 0) bulk_wait_read1();
+          named_bar(2 + wp, 64);
+          float o[16];
+          if (act == XM_ACT_SILU)
+            gate_up_half<XM_ACT_SILU>(v, rs, gate, xg + lane, xu + lane, o);
+          else if (act == XM_ACT_GELU)
+            gate_up_half<XM_ACT_GELU>(v, rs, gate, xg + lane, xu + lane, o);
+          else if (act == XM_ACT_RELU)
+            gate_up_half<XM_ACT_RELU>(v, rs, gate, xg + lane, xu + lane, o);
+          else
+            gate_up_half<XM_ACT_IDENTITY>(v, rs, gate, xg + lane, xu + lane, o);
+          const int c0 = gate ? 0 : 16;
+          if (tma_ok) {
+#pragma unroll
+            for (int c = 0; c < 16; ++c) box[(c0 + c) * 32 + lane] = o[c];
+            fence_proxy_async_smem();
+            named_bar(2 + wp, 64);                // both halves written (and xg / xu read)
+            if (gate && lane == 0) {
+              tma_store_2d(&map_y, box, f0, tok0);
+              bulk_commit();
+            }
+            nb ^= 1;
+          } else {
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              const int tok = tok0 + c0 + c;
+              if (tok < pt.mhi && fok) y[(int64_t)tok * N + f] = o[c];
+            }
+            named_bar(2 + wp, 64);                // xg / xu read before the next chunk writes them
+          }
+          continue;
+        }
+        const float vs = rs;
         if (y_tma && (NMAP == 1 || tok0 + 32 <= pt.mhi)) {
           float* box = box0 + nb * kTmEpiBox;
           if (lane == 0) bulk_wait_read1();       // the store issued from this box two chunks ago has read it
           __syncwarp();
 #pragma unroll
-          for (int c = 0; c < 32; ++c) box[c * 32 + lane] = __uint_as_float(v[c]) * __shfl_sync(~0u, rs, c) + bv;
+          for (int c = 0; c < 32; ++c) box[c * 32 + lane] = __uint_as_float(v[c]) * __shfl_sync(~0u, vs, c) + bv;
           fence_proxy_async_smem();               // generic-proxy writes -> visible to the bulk copy
           __syncwarp();
           if (lane == 0) {
@@ -1386,7 +1463,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         } else {
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
-            const float o = __uint_as_float(v[c]) * __shfl_sync(~0u, rs, c) + bv;
+            const float o = __uint_as_float(v[c]) * __shfl_sync(~0u, vs, c) + bv;
             const int tok = tok0 + c;
             if (tok < pt.mhi && fok) {
               float* yp = y + (int64_t)tok * N + f;
@@ -1721,8 +1798,9 @@ struct TmCfg {
   int NT, nacc, S, RW, smem;
 };
 
-int tm_smem_bytes(int NT, int S, int RW, int BB) {
-  return 1024 + S * (NT / 2) * 256 + kPairEpiWarps * 2 * kTmEpiBox * 4 + RW * kTmRows * BB + (int)sizeof(TmSmem);
+int tm_smem_bytes(int NT, int S, int RW, int BB, bool gu = false) {
+  return 1024 + S * (NT / 2) * 256 + kPairEpiWarps * 2 * kTmEpiBox * 4 + (gu ? 2 * kTmEpiBox * 4 : 0) +
+         RW * kTmRows * BB + (int)sizeof(TmSmem);
 }
 
 // fp32 output [rows][n] as a tensor map with 32 x 32 boxes; false when the
@@ -1744,17 +1822,17 @@ bool encode_y_map(CUtensorMap* map, const float* y, int64_t rows, int64_t n) {
 // they fit beside 4 A stages (so the epilogue of one tile overlaps the next
 // tile's main loop), then as many A stages (<= 6) as tensor and shared memory
 // hold.  S = 0 if fewer than 3 stages fit.
-TmCfg tm_stages(int NT, int BB) {
+TmCfg tm_stages(int NT, int BB, bool gu = false) {
   const int nacc = 2 * NT + 4 * 64 <= 512 ? 2 : 1;
   int S = std::min(kTmMaxStages, (512 - nacc * NT) / 64);
-  while (S >= 3 && tm_smem_bytes(NT, S, kPairRaw, BB) > 227 * 1024) --S;
+  while (S >= 3 && tm_smem_bytes(NT, S, kPairRaw, BB, gu) > 227 * 1024) --S;
   if (S < 3) S = 0;
-  return {NT, nacc, S, kPairRaw, tm_smem_bytes(NT, S, kPairRaw, BB)};
+  return {NT, nacc, S, kPairRaw, tm_smem_bytes(NT, S, kPairRaw, BB, gu)};
 }
 
-template <int T, int NMAP>
+template <int T, int NMAP, bool GU = false>
 const void* tm_kernel() {
-  return reinterpret_cast<const void*>(k_qgemm_tm<T, NMAP>);
+  return reinterpret_cast<const void*>(k_qgemm_tm<T, NMAP, GU>);
 }
 
 // Token tile for m rows (per group) and n output features: estimated clocks
@@ -1762,14 +1840,14 @@ const void* tm_kernel() {
 // 128-K stage costs the larger of its MMA time (4 NT clocks) and the issuing
 // thread's cost (8 MMA issues and a barrier wait beside 16 decode warps,
 // ~1120 clocks measured); the epilogue ~1400 + 20 NT clocks.
-TmCfg choose_tm(int64_t m, int64_t groups, int64_t n, int64_t k, int pairs, int BB) {
+TmCfg choose_tm(int64_t m, int64_t groups, int64_t n, int64_t k, int pairs, int BB, bool gu = false) {
   TmCfg best{0, 0, 0, 0, 0};
   double best_t = 1e30;
   const double nks = (double)(k / kTmStageK);
-  const int64_t tw = (n + 255) / 256;
+  const int64_t tw = gu ? (n + kTmRows - 1) / kTmRows : (n + 255) / 256;
   for (int nt = 256; nt >= 32; nt -= 32) {
     if (nt > 32 && nt - 32 >= m) continue;      // a smaller tile already holds every row
-    const TmCfg c = tm_stages(nt, BB);
+    const TmCfg c = tm_stages(nt, BB, gu);
     if (c.S < 3) continue;
     const int64_t tiles = groups * tw * ((m + nt - 1) / nt);
     const double rounds = (double)((tiles + pairs - 1) / pairs);
@@ -1784,11 +1862,11 @@ TmCfg choose_tm(int64_t m, int64_t groups, int64_t n, int64_t k, int pairs, int 
   return best;
 }
 
-template <int T, int NMAP>
-int launch_tm(const CUtensorMap& map_b, const PairW<NMAP>& pw, int64_t m, int64_t n, int64_t k, int tm,
-              const TmCfg& cfg, int pairs, const float* rowscale, const float* bias, float* y, int acc,
-              cudaStream_t st) {
-  const void* fn = tm_kernel<T, NMAP>();
+template <int T, int NMAP, bool GU = false>
+int launch_tm(const CUtensorMap& map_b, const PairW<NMAP>& pw, const PairW<NMAP>& pw3, int64_t m, int64_t n,
+              int64_t k, int tm, const TmCfg& cfg, int pairs, const float* rowscale, const float* bias, float* y,
+              int acc, int act, cudaStream_t st) {
+  const void* fn = tm_kernel<T, NMAP, GU>();
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, cfg.smem);
   if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemm: smem attribute: %s", cudaGetErrorString(e));
   cudaLaunchConfig_t lc = {};
@@ -1808,8 +1886,8 @@ int launch_tm(const CUtensorMap& map_b, const PairW<NMAP>& pw, int64_t m, int64_
   CUtensorMap map_y;
   memset(&map_y, 0, sizeof(map_y));
   const int y_tma = encode_y_map(&map_y, y, m, n) ? 1 : 0;
-  e = cudaLaunchKernelEx(&lc, k_qgemm_tm<T, NMAP>, map_b, pw, map_y, y_tma, (int)m, (int)n, (int)k, cfg.NT,
-                         cfg.nacc, cfg.S, cfg.RW, tm, rowscale, bias, y, acc);
+  e = cudaLaunchKernelEx(&lc, k_qgemm_tm<T, NMAP, GU>, map_b, pw, pw3, map_y, y_tma, (int)m, (int)n, (int)k,
+                         cfg.NT, cfg.nacc, cfg.S, cfg.RW, tm, rowscale, bias, y, acc, act);
   if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemm tm launch: %s", cudaGetErrorString(e));
   return xm_check_launch("qgemm tm");
 }
@@ -1838,7 +1916,7 @@ int launch_tm_gemm(const __half* a16, const uint8_t* w, int64_t m, int64_t n, in
   const int64_t tm = (m + cfg.NT - 1) / cfg.NT;
   const int64_t tiles = tm * ((n + 255) / 256);
   const int pairs = (int)std::min<int64_t>(tiles, cap_cfg);
-  return launch_tm<T, 1>(map_b, pw, m, n, k, (int)tm, cfg, pairs, rowscale, bias, y, acc, st);
+  return launch_tm<T, 1>(map_b, pw, pw, m, n, k, (int)tm, cfg, pairs, rowscale, bias, y, acc, 0, st);
 }
 
 template <int T>
@@ -1868,7 +1946,39 @@ int launch_tm_grouped(const __half* a16, const uint8_t* const* h_w, const int* d
   const int tm = (int)((max_rows + cfg.NT - 1) / cfg.NT);
   const int64_t tiles = (int64_t)G * tm * ((n + 255) / 256);
   const int pairs = (int)std::min<int64_t>(tiles, cap_cfg);
-  return launch_tm<T, kMaxGroups>(map_b, pw, P, n, k, tm, cfg, pairs, rowscale, nullptr, y, 0, st);
+  return launch_tm<T, kMaxGroups>(map_b, pw, pw, P, n, k, tm, cfg, pairs, rowscale, nullptr, y, 0, 0, st);
+}
+
+// Gate/up experts on the tensor-memory-A kernel: y = act(x W1^T) * (x W3^T)
+// per group (rows [off[g], off[g] + cnt[g])); 1 if the device cannot hold it.
+template <int T>
+int launch_tm_grouped_gu(const __half* a16, const uint8_t* const* h_w1, const uint8_t* const* h_w3, const int* d_cnt,
+                         const int* d_off, int G, int64_t P, int64_t n, int64_t k, int64_t max_rows,
+                         int64_t expect_rows, const float* rowscale, int act, float* y, cudaStream_t st) {
+  constexpr int BB = ColGeom<T>::BB;
+  const void* fn = tm_kernel<T, kMaxGroups, true>();
+  const TmCfg probe = tm_stages(128, BB, true);
+  const int cap = cluster_capacity(fn, kTmThreads, probe.smem);
+  if (cap < 1) return 1;
+  const TmCfg cfg = choose_tm(expect_rows, G, n, k, cap, BB, true);
+  if (cfg.S < 3) return 1;
+  const int cap_cfg = cluster_capacity(fn, kTmThreads, cfg.smem);
+  if (cap_cfg < 1) return 1;
+  CUtensorMap map_b;
+  int rc = encode_a16(&map_b, a16, P, k, cfg.NT / 2);
+  if (rc) return rc;
+  PairW<kMaxGroups> pw1{}, pw3{};
+  for (int g = 0; g < G; ++g) {
+    if ((rc = encode_w_records<T>(&pw1.map[g], h_w1[g], n, k, kTmRows / 2))) return rc;
+    if ((rc = encode_w_records<T>(&pw3.map[g], h_w3[g], n, k, kTmRows / 2))) return rc;
+  }
+  pw1.cnt = pw3.cnt = d_cnt;
+  pw1.off = pw3.off = d_off;
+  pw1.groups = pw3.groups = G;
+  const int tm = (int)((max_rows + cfg.NT - 1) / cfg.NT);
+  const int64_t tiles = (int64_t)G * tm * ((n + kTmRows - 1) / kTmRows);
+  const int pairs = (int)std::min<int64_t>(tiles, cap_cfg);
+  return launch_tm<T, kMaxGroups, true>(map_b, pw1, pw3, P, n, k, tm, cfg, pairs, rowscale, nullptr, y, 0, act, st);
 }
 
 // Runtime type id -> the launchers above (dispatch_quant calls operator()<T>).
@@ -1906,6 +2016,23 @@ struct PairGrouped {
     rc = launch_tm_grouped<T>(a16, h_w, cnt, off, G, P, n, k, max_rows, expect_rows, rowscale, y, st);
     if (rc == 1)
       rc = launch_pair_grouped<T>(*map_a, h_w, cnt, off, G, P, n, k, max_rows, expect_rows, rowscale, y, st);
+  }
+};
+
+struct TmGroupedGU {
+  const __half* a16;
+  const uint8_t *const *w1, *const *w3;
+  const int *cnt, *off;
+  int G;
+  int64_t P, n, k, max_rows, expect_rows;
+  const float* rowscale;
+  int act;
+  float* y;
+  cudaStream_t st;
+  int rc = 1;
+  template <int T>
+  void operator()() {
+    rc = launch_tm_grouped_gu<T>(a16, w1, w3, cnt, off, G, P, n, k, max_rows, expect_rows, rowscale, act, y, st);
   }
 };
 
@@ -1958,6 +2085,19 @@ int qgemm_grouped(int qtype, const __half* a16, const float* rowscale, int64_t P
   const dim3 grid((unsigned)((N + cfg.BN - 1) / cfg.BN), (unsigned)((max_rows + cfg.MT * 128 - 1) / (cfg.MT * 128)),
                   (unsigned)G);
   return launch_gemm(map_a, nullptr, P, N, K, cfg, grid, rowscale, nullptr, y, 0, groups, st);
+}
+
+int qgemm_grouped_gate_up(int qtype, int act, const __half* a16, const float* rowscale, int64_t P, int64_t K,
+                          int64_t N, const uint8_t* const* h_w1, const uint8_t* const* h_w3, const int* d_cnt,
+                          const int* d_off, int G, int64_t max_rows, int64_t expect_rows, float* y, cudaStream_t st) {
+  if (K % 256 || K < 256 || N < 1 || P < 1 || G < 1 || G > kMaxGroups)
+    return xm_set_error(XM_ERR_INVALID, "grouped gate/up qgemm: bad shape");
+  if (!qgemm_type_supported(qtype, K))
+    return xm_set_error(XM_ERR_UNSUPPORTED, "grouped gate/up qgemm: type id %d rows of k=%lld are not 16-byte "
+                        "multiples", qtype, (long long)K);
+  TmGroupedGU g{a16, h_w1, h_w3, d_cnt, d_off, G, P, N, K, max_rows, expect_rows, rowscale, act, y, st};
+  dispatch_quant(qtype, g);
+  return g.rc;
 }
 
 extern "C" int64_t xm_qgemm_workspace_size(int64_t m, int64_t k) {
