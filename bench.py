@@ -510,7 +510,7 @@ def run_ours(args):
             tf = flops * reps_g / (ms / 1e3) / 1e12
             us = ms * 1e3 / reps_g
             sweep[f"M={mm}"] = {"TFLOPS": round(tf, 1), "us": round(us, 2),
-                                "kernel": "tcgen05 CTA-pair GEMM" if mm > 8 else "integer mma.sync GEMV",
+                                "kernel": "tcgen05 GEMM (CTA pairs, decoded weights in tensor memory)" if mm > 8 else "integer mma.sync GEMV",
                                 "frac_of_measured_bf16_peak": round(tf / float(peaks.get("bf16_tflops", 1590.0)), 4),
                                 "weight_GBps": round(W_BYTES / us / 1e3, 1)}
 

@@ -1030,7 +1030,14 @@ __global__ void __launch_bounds__(pair_threads(DW), 1)
 // MMAs (K = 16 each) per barrier wait, since a wait on the issuing thread
 // costs about as much as issuing two MMAs and small-N MMAs are issue-bound.
 // Tensor memory (512 columns per CTA): nacc accumulators of NT columns, then
-// S stages of 64 columns of A (128 K values x 128 rows).
+// S stages of 64 columns of A (128 K values x 128 rows).  With one accumulator
+// of more than 128 columns (nacc = 0, "ping-pong": S = 4 and 4 | K/128), the
+// accumulator of tile t and the A stages swap halves on every tile: D_t in
+// columns 256 (t & 1) .. +NT, stage s of tile t in 256 (1 - (t & 1)) + 64 s,
+// which is where chunks 2s, 2s + 1 of D_(t-1) lie; the epilogue frees each
+// 64-column slot (col_free[s]) as soon as it has read it, and the decode warps
+// wait for that before the first write of the slot in a tile, so the next
+// tile's main loop runs while the epilogue drains.
 //
 // Warps (24 per CTA):
 //   0        TMA producer of the activation tiles, two 64-K boxes per stage
@@ -1067,9 +1074,9 @@ struct TmSmem {
   uint64_t wfull[kMaxRawStages], wempty[kMaxRawStages];
   uint64_t ofull[kTmMaxStages], oempty[kTmMaxStages];
   uint64_t acc_full[2], acc_empty[2];
+  uint64_t col_free[4];            // ping-pong mode: the epilogue has read these 64 columns of the last tile
   uint32_t tmem_base;
 };
-
 
 XM_DEV void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
@@ -1213,7 +1220,8 @@ __global__ void __launch_bounds__(kTmThreads, 1)
   const int TW = (N + TWID - 1) / TWID;
   const int NTILES = TM * TW * (NMAP == 1 ? 1 : pw.groups);
   const int KB = K >> 8, nks = K / kTmStageK;
-  const uint32_t a_col0 = (uint32_t)(nacc * NT);  // first tensor-memory column of the A stages
+  const bool pp = nacc == 0;                      // ping-pong accumulator (see above)
+  const uint32_t a_col0 = (uint32_t)(nacc * NT);  // first tensor-memory column of the A stages (nacc > 0)
 
   if (tid == 0) {
     for (int i = 0; i < RW; ++i) {
@@ -1228,6 +1236,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
       mbar_init(&ctl->acc_full[b], 1);
       mbar_init(&ctl->acc_empty[b], 2 * kPairEpiWarps);
     }
+    for (int i = 0; i < 4; ++i) mbar_init(&ctl->col_free[i], kPairEpiWarps);   // this CTA's epilogue warps
     fence_mbar_init();
   }
   constexpr uint32_t kCols = 512;
@@ -1279,15 +1288,16 @@ __global__ void __launch_bounds__(kTmThreads, 1)
       for (int t = pair; t < NTILES; t += npairs) {
         PairTile pt;
         if (!tm_tile(pw, t, M, TM, TW, NT, TWID, pt)) continue;
-        const uint32_t b = nacc == 2 ? (it & 1) : 0u, u = nacc == 2 ? (it >> 1) : it;
-        pair_wait(&ctl->acc_empty[b], (u & 1) ^ 1);
+        const uint32_t b = nacc != 1 ? (it & 1) : 0u, u = nacc != 1 ? (it >> 1) : it;
+        if (!pp) pair_wait(&ctl->acc_empty[b], (u & 1) ^ 1);   // (ping-pong: the decode warps' col_free waits)
         tc_fence_after();
-        const uint32_t d = tmem + b * (uint32_t)NT;
+        const uint32_t d = pp ? tmem + (it & 1u) * 256u : tmem + b * (uint32_t)NT;
+        const uint32_t abase = pp ? tmem + ((it & 1u) ^ 1u) * 256u : tmem + a_col0;
         for (int ks = 0; ks < nks; ++ks) {
           pair_wait(&ctl->ofull[s], ph);
           tc_fence_after();
           const uint64_t bs = b0 + s * bstep;
-          tc2_mma_stage128(d, tmem + a_col0 + s * 64u, (uint32_t)bs, (uint32_t)(bs >> 32), (uint32_t)bh, idesc,
+          tc2_mma_stage128(d, abase + s * 64u, (uint32_t)bs, (uint32_t)(bs >> 32), (uint32_t)bh, idesc,
                            ks == 0 ? 1u : 0u);
           tc2_commit_pair(&ctl->oempty[s]);      // both CTAs may refill the stage once these MMAs are done
           if (++s == (uint32_t)S) { s = 0; ph ^= 1; }
@@ -1324,16 +1334,21 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     const int quarter = warp & 3;                 // the tensor-memory lanes this warp may access
     const int row = quarter * 32 + lane;          // this thread's weight row in the CTA's 128
     const uint32_t leader_ofull = mapa_shared(smem_u32(&ctl->ofull[0]), 0);
-    const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16) + a_col0 + (uint32_t)(hs * 32);
+    const uint32_t lane0 = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(hs * 32);
     uint32_t s = (uint32_t)grp, ph = 0, rs = 0, rph = 0;   // this group's first stage is q = grp (< S)
+    uint32_t it = 0;
     for (int t = pair; t < NTILES; t += npairs) {
       PairTile pt;
       if (!tm_tile(pw, t, M, TM, TW, NT, TWID, pt)) continue;
+      const uint32_t lane_addr = lane0 + (pp ? ((it & 1u) ^ 1u) * 256u : a_col0);
       for (int kb = 0; kb < KB; ++kb) {
         pair_wait(&ctl->wfull[rs], rph);
         const int mis = (kb * CG::CB) & 15;       // the column's offset in its staged box (0 for Q4_K)
         const uint8_t* rec = sW + rs * wstage + row * CG::BB + mis;
         pair_wait(&ctl->oempty[s], ph ^ 1);       // the MMAs that read these columns are done
+        // ping-pong: the first write of a slot in a tile also waits for the
+        // epilogue of the previous tile to have read these columns
+        if (pp && it > 0 && kb < 2) pair_wait(&ctl->col_free[s], (it - 1u) & 1u);
         tc_fence_after();
         uint32_t hv[16];
         item_regs<T>(rec, j, 0, hv);
@@ -1354,6 +1369,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         if (s >= (uint32_t)S) { s -= (uint32_t)S; ph ^= 1; }
         if (++rs == (uint32_t)RW) { rs = 0; rph ^= 1; }
       }
+      ++it;
     }
   } else if (warp >= 4 + kTmDecodeWarps) {
     // ---------------- epilogue ----------------
@@ -1373,7 +1389,9 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     for (int t = pair; t < NTILES; t += npairs) {
       PairTile pt;
       if (!tm_tile(pw, t, M, TM, TW, NT, TWID, pt)) continue;
-      const uint32_t b = nacc == 2 ? (it & 1) : 0u, u = nacc == 2 ? (it >> 1) : it;
+      const uint32_t b = nacc != 1 ? (it & 1) : 0u, u = nacc != 1 ? (it >> 1) : it;
+      const uint32_t dcol = pp ? (it & 1u) * 256u : b * (uint32_t)NT;
+      uint32_t rel = 0;                           // ping-pong: 64-column slots released so far
       const int f0 = pt.col0 + (GU ? (int)rank * (kTmRows / 2) + (quarter & 1) * 32 : (int)rank * kTmRows + quarter * 32);
       const int f = f0 + lane;                    // this thread's output feature
       const bool fok = f < N;
@@ -1394,8 +1412,14 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         const int tok0 = pt.am0 + ch * 32;
         if (ch >= nch || tok0 >= pt.mhi) break;
         uint32_t v[32];
-        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + b * (uint32_t)NT + (uint32_t)(ch * 32), v);
+        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + dcol + (uint32_t)(ch * 32), v);
         tmem_ld_wait();
+        if (pp && (ch & 1)) {                     // chunks 2s, 2s + 1 read: slot s may take A of the next tile
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ctl->col_free[ch >> 1]);
+          rel = (uint32_t)(ch >> 1) + 1u;
+        }
         const float rs = rsv[ch];
         if constexpr (GU) {
           const int wp = quarter & 1;            // warp pair: gate warp wp, up warp wp + 2
@@ -1478,10 +1502,13 @@ __global__ void __launch_bounds__(kTmThreads, 1)
       tc_fence_before();                          // this warp's tensor-memory reads are complete
       __syncwarp();
       if (lane == 0) {
-        if (rank == 0)
+        if (pp) {
+          for (; rel < 4u; ++rel) mbar_arrive(&ctl->col_free[rel]);   // slots of chunks this tile did not have
+        } else if (rank == 0) {
           mbar_arrive(&ctl->acc_empty[b]);
-        else
+        } else {
           mbar_arrive_remote(leader_acc_empty + 8u * b);
+        }
       }
       ++it;
     }
@@ -1822,8 +1849,11 @@ bool encode_y_map(CUtensorMap* map, const float* y, int64_t rows, int64_t n) {
 // they fit beside 4 A stages (so the epilogue of one tile overlaps the next
 // tile's main loop), then as many A stages (<= 6) as tensor and shared memory
 // hold.  S = 0 if fewer than 3 stages fit.
-TmCfg tm_stages(int NT, int BB, bool gu = false) {
+TmCfg tm_stages(int NT, int BB, bool gu = false, bool pp_ok = false) {
   const int nacc = 2 * NT + 4 * 64 <= 512 ? 2 : 1;
+  // one accumulator: ping-pong halves when 4 stages fit (nacc = 0)
+  if (nacc == 1 && pp_ok && tm_smem_bytes(NT, 4, kPairRaw, BB, gu) <= 227 * 1024)
+    return {NT, 0, 4, kPairRaw, tm_smem_bytes(NT, 4, kPairRaw, BB, gu)};
   int S = std::min(kTmMaxStages, (512 - nacc * NT) / 64);
   while (S >= 3 && tm_smem_bytes(NT, S, kPairRaw, BB, gu) > 227 * 1024) --S;
   if (S < 3) S = 0;
@@ -1839,15 +1869,17 @@ const void* tm_kernel() {
 // per pair = rounds x (main loop + the epilogues that do not overlap it).  A
 // 128-K stage costs the larger of its MMA time (4 NT clocks) and the issuing
 // thread's cost (8 MMA issues and a barrier wait beside 16 decode warps,
-// ~1120 clocks measured); the epilogue ~1400 + 20 NT clocks.
+// ~1120 clocks measured); the epilogue ~1400 + 20 NT clocks, hidden behind
+// the next tile except with one non-ping-pong accumulator.
 TmCfg choose_tm(int64_t m, int64_t groups, int64_t n, int64_t k, int pairs, int BB, bool gu = false) {
   TmCfg best{0, 0, 0, 0, 0};
   double best_t = 1e30;
   const double nks = (double)(k / kTmStageK);
+  const bool pp_ok = (k / kTmStageK) % 4 == 0;
   const int64_t tw = gu ? (n + kTmRows - 1) / kTmRows : (n + 255) / 256;
   for (int nt = 256; nt >= 32; nt -= 32) {
     if (nt > 32 && nt - 32 >= m) continue;      // a smaller tile already holds every row
-    const TmCfg c = tm_stages(nt, BB, gu);
+    const TmCfg c = tm_stages(nt, BB, gu, pp_ok);
     if (c.S < 3) continue;
     const int64_t tiles = groups * tw * ((m + nt - 1) / nt);
     const double rounds = (double)((tiles + pairs - 1) / pairs);
