@@ -152,6 +152,24 @@ def test_gemm_swiglu_prologue_accumulate(name):
     assert rel_err(y.cpu().numpy(), ref) < GEMM_TOL
 
 
+@pytest.mark.parametrize("name", ["Q4_K", "Q8_0", "Q6_K"])
+@pytest.mark.parametrize("accumulate", [False, True])
+def test_gemm_many_tiles_per_pair(name, accumulate):
+    """Several 256-token tiles per CTA pair (5 token tiles x 36 feature tiles over 74 pairs), so the
+    accumulator is drained and refilled between tiles inside one launch: with bias, and as the
+    residual add (y += x W^T + b).  Q8_0 records stage with fewer pipeline stages."""
+    m, n, k = 1200, 9216, 2048
+    raw, w = wref(name, n, k, 97)
+    rng = np.random.default_rng(98)
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(99)).to(torch.bfloat16)   # exact in fp16
+    b = rng.standard_normal(n).astype(np.float32)
+    h0 = rng.standard_normal((m, n)).astype(np.float32) if accumulate else np.zeros((m, n), np.float32)
+    y = torch.from_numpy(h0.copy()).cuda()
+    _gemm(GGUFTensor(raw, name, (n, k)), x.cuda(), y=y, accumulate=accumulate, bias=torch.from_numpy(b).cuda())
+    ref = h0 + x.float().numpy() @ w.T + b
+    assert rel_err(y.cpu().numpy(), ref) < 1e-5, rel_err(y.cpu().numpy(), ref)
+
+
 def test_gemm_row_pitch_not_16_bytes_falls_back_to_gemv():
     """Q6_K rows of 1792 (a tensor-parallel K-slice of 14336 over 8 ranks) are 1470 bytes: the
     GEMM reports UNSUPPORTED and qlinear multiplies them on the GEMV in groups of 8 rows."""
