@@ -280,7 +280,8 @@ int xm_qgemv_noalloc(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int
  * (vocab rows of D) -- the reference indexes its dequantized embedding
  * (forward.py:151).
  *
- * xm_attention: causal GQA attention of Lq (<= 64) new tokens per sequence.
+ * xm_attention: causal GQA attention of Lq new tokens per sequence (Lq <= 64, or
+ * any Lq >= 16 when both row pitches are even: the prefill path, tensor cores).
  * qkv row b*Lq + j = [q | k | v] (Hq, Hk, Hk heads, fp32, row pitch
  * qkv_stride) of token j of sequence b at position pos0[b] + j, as the QKV
  * projection produced it.  Fused: rotate-half rotary embedding of q and k

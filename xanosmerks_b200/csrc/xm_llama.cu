@@ -261,6 +261,228 @@ __global__ void __launch_bounds__(256) k_attention(const float* __restrict__ qkv
   if (tid == 0) tickets[bh] = 0;   // ready for the next call
 }
 
+// ---------------------------------------------------------------------------
+// Prefill attention (16 or more new tokens per sequence): first the new
+// tokens' keys and values are rotated and appended to the cache
+// (k_kv_append, the same rotation and fp16 rounding as k_attention), then
+// k_attn_chunk computes causal GQA attention from the cache on tensor cores
+// (mma.sync m16n8k16, fp16 operands, fp32 accumulation, online softmax).
+//
+// CTA (b, hk, t): KV head hk of sequence b and new tokens 16t .. 16t + 15;
+// warp g computes query head hk * G + g for those 16 tokens (the C fragment
+// rows).  The CTA walks the keys 0 .. pos0 + last token in tiles of 64,
+// staged in shared memory ([key][dim], 272-byte rows so that ldmatrix reads
+// eight rows without bank conflicts) and shared by the G warps.  S = q k^T
+// (q rotated and scaled by log2(e) / sqrt(128) in registers, fp16), the
+// running max and sum per row, P (fp16) reuses the S fragments as the A
+// operand of P V (ldmatrix.trans of the V rows), and O / l is written as fp32.
+// Keys past the last written position read as zeros in shared memory and are
+// masked, so no uninitialised cache entry enters a product.
+// ---------------------------------------------------------------------------
+constexpr int kChunkTok = 16;           // new tokens per CTA (the MMA's M)
+constexpr int kKeyTile = 64;
+constexpr int kRowH = kHeadDim + 8;     // halves per staged row (272 bytes)
+
+__global__ void __launch_bounds__(128) k_kv_append(const float* __restrict__ qkv, int64_t qkv_stride,
+                                                   __half* __restrict__ kc, __half* __restrict__ vc,
+                                                   const int* __restrict__ pos0, int Lq, int Hq, int Hk,
+                                                   int max_ctx, float theta) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int row = blockIdx.x, b = row / Lq, j = row % Lq;
+  const int pos = pos0[b] + j;
+  const float* r = qkv + (int64_t)row * qkv_stride + (int64_t)Hq * kHeadDim;
+  for (int i = threadIdx.x; i < Hk * (kHeadDim / 2); i += blockDim.x) {
+    const int hk = i / (kHeadDim / 2), d = i % (kHeadDim / 2);
+    float ka = r[hk * kHeadDim + d], kb = r[hk * kHeadDim + d + 64];
+    rope_pair(ka, kb, pos, d, theta);
+    const float va = r[(Hk + hk) * kHeadDim + d], vb = r[(Hk + hk) * kHeadDim + d + 64];
+    const int64_t at = (((int64_t)b * Hk + hk) * max_ctx + pos) * kHeadDim;
+    kc[at + d] = __float2half_rn(ka);
+    kc[at + d + 64] = __float2half_rn(kb);
+    vc[at + d] = __float2half_rn(va);
+    vc[at + d + 64] = __float2half_rn(vb);
+  }
+}
+
+XM_DEV uint32_t pack_half2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+XM_DEV void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+XM_DEV void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+XM_DEV void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+
+__global__ void __launch_bounds__(32 * kMaxGroup) k_attn_chunk(const float* __restrict__ qkv, int64_t qkv_stride,
+                                                               const __half* __restrict__ kc,
+                                                               const __half* __restrict__ vc,
+                                                               const int* __restrict__ pos0, int Lq, int Hq, int Hk,
+                                                               int max_ctx, float theta, float* __restrict__ out,
+                                                               int64_t out_stride) {
+  __shared__ __align__(16) __half ks[kKeyTile][kRowH];
+  __shared__ __align__(16) __half vs[kKeyTile][kRowH];
+  grid_dep_wait();                                 // the appended keys come from the preceding kernel
+  grid_dep_launch();
+  const int b = blockIdx.x / Hk, hk = blockIdx.x % Hk;
+  const int j0 = ((int)gridDim.y - 1 - (int)blockIdx.y) * kChunkTok;   // the longest (last) tiles start first
+  const int G = Hq / Hk;
+  const int tid = threadIdx.x, lane = tid & 31, g = tid >> 5;
+  const int nthr = blockDim.x;
+  const int p0 = pos0[b];
+  const int jlast = min(j0 + kChunkTok, Lq) - 1;
+  const int kend = p0 + jlast + 1;                 // keys this CTA's last token sees
+  const int64_t bh = (int64_t)b * Hk + hk;
+  const __half* K = kc + bh * max_ctx * kHeadDim;
+  const __half* V = vc + bh * max_ctx * kHeadDim;
+  const int r0 = lane >> 2, c2 = 2 * (lane & 3);   // fragment row (and row + 8), column pair
+  // this lane's two tokens (rows r0, r0 + 8; rows past the last token repeat it and are not written)
+  const int ja = min(j0 + r0, Lq - 1), jb = min(j0 + r0 + 8, Lq - 1);
+  const int posa = p0 + ja, posb = p0 + jb;
+
+  // q fragments: k-step s covers dims 16s .. 16s + 15; this lane holds dims 16s + c2 (+1) and
+  // 16s + 8 + c2 (+1) of rows a and b, so dims d and d + 64 (steps s and s + 4) meet in one lane
+  uint32_t qf[8][4];
+  {
+    const float qscale = 1.4426950408889634f * rsqrtf((float)kHeadDim);   // log2(e) / sqrt(d)
+    const float* qa = qkv + ((int64_t)b * Lq + ja) * qkv_stride + (int64_t)(hk * G + g) * kHeadDim;
+    const float* qb = qkv + ((int64_t)b * Lq + jb) * qkv_stride + (int64_t)(hk * G + g) * kHeadDim;
+#pragma unroll
+    for (int s4 = 0; s4 < 4; ++s4) {
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {            // dims 16 s4 + 8 hf + c2, +1
+        const int d = 16 * s4 + 8 * hf + c2;
+        float a0 = qa[d], a1 = qa[d + 1], a0h = qa[d + 64], a1h = qa[d + 65];
+        float b0 = qb[d], b1 = qb[d + 1], b0h = qb[d + 64], b1h = qb[d + 65];
+        rope_pair(a0, a0h, posa, d, theta);
+        rope_pair(a1, a1h, posa, d + 1, theta);
+        rope_pair(b0, b0h, posb, d, theta);
+        rope_pair(b1, b1h, posb, d + 1, theta);
+        qf[s4][2 * hf] = pack_half2(a0 * qscale, a1 * qscale);
+        qf[s4][2 * hf + 1] = pack_half2(b0 * qscale, b1 * qscale);
+        qf[s4 + 4][2 * hf] = pack_half2(a0h * qscale, a1h * qscale);
+        qf[s4 + 4][2 * hf + 1] = pack_half2(b0h * qscale, b1h * qscale);
+      }
+    }
+  }
+  float o[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float ma = -INFINITY, mb = -INFINITY, la = 0.f, lb = 0.f;
+  const uint32_t ks0 = (uint32_t)__cvta_generic_to_shared(&ks[0][0]);
+  const uint32_t vs0 = (uint32_t)__cvta_generic_to_shared(&vs[0][0]);
+  const int mi = lane >> 3, mr = lane & 7;        // ldmatrix: this lane addresses row mr of matrix mi
+
+  for (int kb = 0; kb < kend; kb += kKeyTile) {
+    __syncthreads();                               // the previous tile is no longer read
+    for (int i = tid; i < kKeyTile * (kHeadDim / 8); i += nthr) {
+      const int r = i / (kHeadDim / 8), c = (i % (kHeadDim / 8)) * 8;
+      const int key = kb + r;
+      uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+      if (key < kend) {
+        kv = *reinterpret_cast<const uint4*>(K + (int64_t)key * kHeadDim + c);
+        vv = *reinterpret_cast<const uint4*>(V + (int64_t)key * kHeadDim + c);
+      }
+      *reinterpret_cast<uint4*>(&ks[r][c]) = kv;
+      *reinterpret_cast<uint4*>(&vs[r][c]) = vv;
+    }
+    __syncthreads();
+    // S = q k^T: 8 tiles of 8 keys
+    float sc[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {            // key tiles 2np, 2np + 1
+        // matrices: (keys 16np..+7, dims 16s..+7), (same keys, dims +8), (keys +8, dims 16s), (keys +8, dims +8)
+        const int key = 16 * np + mr + 8 * (mi >> 1), dim = 16 * s + 8 * (mi & 1);
+        uint32_t k0, k1, k2, k3;
+        ldsm_x4(ks0 + (uint32_t)(key * kRowH + dim) * 2u, k0, k1, k2, k3);
+        mma_f16_16816(sc[2 * np], qf[s], k0, k1);
+        mma_f16_16816(sc[2 * np + 1], qf[s], k2, k3);
+      }
+    }
+    // mask (causal, and keys not yet written), online softmax
+    float tma = -INFINITY, tmb = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const int key = kb + 8 * n + c2;
+      if (key > posa) sc[n][0] = -INFINITY;
+      if (key + 1 > posa) sc[n][1] = -INFINITY;
+      if (key > posb) sc[n][2] = -INFINITY;
+      if (key + 1 > posb) sc[n][3] = -INFINITY;
+      tma = fmaxf(tma, fmaxf(sc[n][0], sc[n][1]));
+      tmb = fmaxf(tmb, fmaxf(sc[n][2], sc[n][3]));
+    }
+    tma = fmaxf(tma, __shfl_xor_sync(~0u, tma, 1));
+    tma = fmaxf(tma, __shfl_xor_sync(~0u, tma, 2));
+    tmb = fmaxf(tmb, __shfl_xor_sync(~0u, tmb, 1));
+    tmb = fmaxf(tmb, __shfl_xor_sync(~0u, tmb, 2));
+    const float na = fmaxf(ma, tma), nb = fmaxf(mb, tmb);   // finite: key 0 is always visible
+    const float aa = exp2f(ma - na), ab = exp2f(mb - nb);
+    ma = na;
+    mb = nb;
+    float suma = 0.f, sumb = 0.f;
+    uint32_t pf[4][4];                              // P as the A operand: k-step s = key tiles 2s, 2s + 1
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const float e0 = exp2f(sc[n][0] - na), e1 = exp2f(sc[n][1] - na);
+      const float e2 = exp2f(sc[n][2] - nb), e3 = exp2f(sc[n][3] - nb);
+      suma += e0 + e1;
+      sumb += e2 + e3;
+      pf[n >> 1][2 * (n & 1)] = pack_half2(e0, e1);
+      pf[n >> 1][2 * (n & 1) + 1] = pack_half2(e2, e3);
+    }
+    la = la * aa + suma;
+    lb = lb * ab + sumb;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      o[n][0] *= aa;
+      o[n][1] *= aa;
+      o[n][2] *= ab;
+      o[n][3] *= ab;
+    }
+    // O += P V: 4 k-steps of 16 keys, 16 tiles of 8 dims
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+#pragma unroll
+      for (int dp = 0; dp < 8; ++dp) {            // dim tiles 2dp, 2dp + 1
+        // matrices (transposed): (keys 16s..+7, dims 16dp..+7), (keys +8, same dims), (keys 16s, dims +8), (keys +8, dims +8)
+        const int key = 16 * s + mr + 8 * (mi & 1), dim = 16 * dp + 8 * (mi >> 1);
+        uint32_t v0, v1, v2, v3;
+        ldsm_x4_t(vs0 + (uint32_t)(key * kRowH + dim) * 2u, v0, v1, v2, v3);
+        mma_f16_16816(o[2 * dp], pf[s], v0, v1);
+        mma_f16_16816(o[2 * dp + 1], pf[s], v2, v3);
+      }
+    }
+  }
+  // row sums across the quad, then O / l
+  la += __shfl_xor_sync(~0u, la, 1);
+  la += __shfl_xor_sync(~0u, la, 2);
+  lb += __shfl_xor_sync(~0u, lb, 1);
+  lb += __shfl_xor_sync(~0u, lb, 2);
+  const float ia = 1.0f / la, ib = 1.0f / lb;
+  const bool wa = j0 + r0 < Lq, wb = j0 + r0 + 8 < Lq;
+  float* oa = out + ((int64_t)b * Lq + ja) * out_stride + (int64_t)(hk * G + g) * kHeadDim;
+  float* ob = out + ((int64_t)b * Lq + jb) * out_stride + (int64_t)(hk * G + g) * kHeadDim;
+#pragma unroll
+  for (int n = 0; n < 16; ++n) {
+    if (wa) *reinterpret_cast<float2*>(oa + 8 * n + c2) = make_float2(o[n][0] * ia, o[n][1] * ia);
+    if (wb) *reinterpret_cast<float2*>(ob + 8 * n + c2) = make_float2(o[n][2] * ib, o[n][3] * ib);
+  }
+}
+
 // first index of the maximum of each row (np.argmax semantics; NaN-free
 // input).  One CTA per row; 16-byte loads, eight in flight per thread.
 XM_DEV void argmax_take(float v, int i, float& best, int& idx) {
@@ -354,7 +576,9 @@ int xm_attention(const float* d_qkv, int64_t qkv_stride, void* d_kcache, void* d
                  int Lq, int Hq, int Hk, int head_dim, float theta, int64_t max_ctx, float* d_out,
                  int64_t out_stride, void* d_workspace, int64_t workspace_bytes, void* stream) {
   if (head_dim != kHeadDim) return xm_set_error(XM_ERR_UNSUPPORTED, "attention: head_dim %d (only 128)", head_dim);
-  if (B < 1 || Lq < 1 || Lq > kMaxLq || Hq < 1 || Hk < 1 || Hq % Hk || Hq / Hk > kMaxGroup)
+  // 16 or more new tokens take the prefill path (any count); fewer, the split-key decode kernel (<= 64)
+  const bool chunk = Lq >= kChunkTok && (out_stride % 2) == 0 && (qkv_stride % 2) == 0;
+  if (B < 1 || Lq < 1 || (Lq > kMaxLq && !chunk) || Hq < 1 || Hk < 1 || Hq % Hk || Hq / Hk > kMaxGroup)
     return xm_set_error(XM_ERR_INVALID, "attention: bad head counts (G <= 8) or more than %d new tokens", kMaxLq);
   if (max_ctx < 1 || max_ctx > (1 << 24) || qkv_stride < (int64_t)(Hq + 2 * Hk) * kHeadDim ||
       out_stride < (int64_t)Hq * kHeadDim || !d_qkv || !d_kcache || !d_vcache || !d_pos0 || !d_out)
@@ -367,6 +591,20 @@ int xm_attention(const float* d_qkv, int64_t qkv_stride, void* d_kcache, void* d
   AttnPart* part_ml = (AttnPart*)(part_o + cells * kHeadDim);
   int* tickets = (int*)(part_ml + cells);
   // tickets start at zero (the caller zeroes the workspace once) and every call leaves them at zero
+  if (chunk) {
+    // prefill chunk: append the new keys and values, then tensor-core attention from the cache
+    const int G = Hq / Hk;
+    int rc = launch_status(launch_pdl(k_kv_append, dim3((unsigned)(B * Lq)), dim3(128), (cudaStream_t)stream, d_qkv,
+                                      qkv_stride, (__half*)d_kcache, (__half*)d_vcache, d_pos0, Lq, Hq, Hk,
+                                      (int)max_ctx, theta),
+                           "attention kv append");
+    if (rc) return rc;
+    return launch_status(launch_pdl(k_attn_chunk, dim3((unsigned)(B * Hk), (unsigned)((Lq + kChunkTok - 1) / kChunkTok)),
+                                    dim3((unsigned)(32 * G)), (cudaStream_t)stream, d_qkv, qkv_stride,
+                                    (const __half*)d_kcache, (const __half*)d_vcache, d_pos0, Lq, Hq, Hk,
+                                    (int)max_ctx, theta, d_out, out_stride),
+                         "attention chunk");
+  }
   const unsigned Z = (unsigned)((Lq + kAttnTokensPerCta - 1) / kAttnTokensPerCta);
   return launch_status(launch_pdl(k_attention, dim3((unsigned)(B * Hk), (unsigned)nsplit, Z), dim3(256),
                                   (cudaStream_t)stream, d_qkv, qkv_stride, (__half*)d_kcache, (__half*)d_vcache,

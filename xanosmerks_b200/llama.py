@@ -415,9 +415,17 @@ class LlamaDecoder:
         e = self.w.embed
         check(lib.xm_embed(e.qtype.type_id, e.data.data_ptr(), e.nbytes, e.shape[0], e.shape[1], idv.data_ptr(),
                            rows, h.data_ptr(), st), "embed")
+        # 16 or more tokens: one attention call over all sequences (the tensor-core prefill path)
+        whole = S >= 16
+        zeros_b = torch.zeros(B, dtype=torch.int32, device=self.dev)
         for li, lw in enumerate(self.w.layers):
             self._gemm(lw["qkv"], h, rows, qkv, PRO_RMSNORM, lw["attn_norm"])
-            for b in range(B):
+            if whole:
+                check(lib.xm_attention(qkv.data_ptr(), self.qkv_dim, self.kc[li].data_ptr(), self.vc[li].data_ptr(),
+                                       zeros_b.data_ptr(), B, S, self.hq, self.hk, hd, cfg.rope_theta,
+                                       self.max_ctx, attn.data_ptr(), self.hq * hd, self.attn_ws.data_ptr(),
+                                       self.attn_ws.numel(), st), "attention")
+            for b in range(B if not whole else 0):
                 for ci, c0 in enumerate(range(0, S, self.PREFILL_CHUNK)):
                     lq = min(self.PREFILL_CHUNK, S - c0)
                     r0 = b * S + c0
