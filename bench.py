@@ -488,7 +488,7 @@ def run_ours(args):
                 torch.bfloat16)
             ys = torch.empty((mm, N), dtype=torch.float32, device=dev)
             if mm > 8:
-                gsz = lib.xm_qgemm_workspace_size(mm, K)
+                gsz = lib.xm_qgemm_workspace_size_n(mm, N, K)
             else:
                 gsz = lib.xm_qgemv_workspace_size(K, mm)
             gws = torch.empty(gsz, dtype=torch.uint8, device=dev)
@@ -765,7 +765,7 @@ def run_gemm_only(args):
     mm = args.gemm_m
     xs = torch.from_numpy(np.random.default_rng(5).standard_normal((mm, k)).astype(np.float32)).to(dev).to(torch.bfloat16)
     ys = torch.empty((mm, n), dtype=torch.float32, device=dev)
-    gsz = lib.xm_qgemm_workspace_size(mm, k)
+    gsz = lib.xm_qgemm_workspace_size_n(mm, n, k)
     gws = torch.empty(gsz, dtype=torch.uint8, device=dev)
     st = torch.cuda.current_stream().cuda_stream
 

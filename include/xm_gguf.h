@@ -163,12 +163,18 @@ int xm_qgemv_exact(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64
  * Q3_K rows of k = 1792, for example, are not): other shapes return
  * XM_ERR_UNSUPPORTED and callers use xm_qgemv on groups of 8 rows.
  * `d_workspace` (256-byte aligned, >= xm_qgemm_workspace_size(m, k) bytes)
- * holds the converted activations.
+ * holds the converted activations.  A workspace of
+ * xm_qgemm_workspace_size_n(m, n, k) bytes also holds the partial sums of a
+ * split-K launch, which the GEMM uses when its output tiles are too few to
+ * occupy the device (n % 4 == 0, y and bias 16-byte aligned): each K part
+ * writes its own plane and one kernel adds the planes in a fixed order, so the
+ * result is the same on every run.
  *
  * Replaces the prefill `x @ W.T` of LinearOp.forward (ops.py:62-67) and of
  * the MLP / attention projections (forward.py:93-101, attention.py:47-51).
  */
 int64_t xm_qgemm_workspace_size(int64_t m, int64_t k);
+int64_t xm_qgemm_workspace_size_n(int64_t m, int64_t n, int64_t k);
 int xm_qgemm(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k,
              const void* d_x, int x_dtype, int64_t m, const float* d_bias, float* d_y,
              void* d_workspace, int64_t workspace_bytes, void* stream);

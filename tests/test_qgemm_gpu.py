@@ -73,13 +73,15 @@ def test_qgemm_rejects_bad_arguments():
     assert L.xm_qgemm(14, None, 0, 4, 256, None, 0, 64, None, None, None, 0, None) == _lib.XM_ERR_INVALID  # short
 
 
-def _gemm(W, x, prologue=_lib.PRO_NONE, norm=None, y=None, accumulate=False, eps=1e-5, bias=None):
-    """xm_qgemm_ex on a CUDA activation (fp32 rows of k, or 2k for SwiGLU)."""
+def _gemm(W, x, prologue=_lib.PRO_NONE, norm=None, y=None, accumulate=False, eps=1e-5, bias=None, split=False):
+    """xm_qgemm_ex on a CUDA activation (fp32 rows of k, or 2k for SwiGLU); `split` sizes the
+    workspace for split-K partial planes."""
     n, k = W.shape
     m = x.shape[0]
     if y is None:
         y = torch.zeros(m, n, dtype=torch.float32, device="cuda")
-    ws = torch.empty(_lib.lib.xm_qgemm_workspace_size(m, k), dtype=torch.uint8, device="cuda")
+    wsz = _lib.lib.xm_qgemm_workspace_size_n(m, n, k) if split else _lib.lib.xm_qgemm_workspace_size(m, k)
+    ws = torch.empty(wsz, dtype=torch.uint8, device="cuda")
     dt = {torch.float32: _lib.DT_F32, torch.bfloat16: _lib.DT_BF16, torch.float16: _lib.DT_F16}[x.dtype]
     _lib.check(_lib.lib.xm_qgemm_ex(W.qtype.type_id, W.data.data_ptr(), W.nbytes, n, k, x.data_ptr(), dt, m,
                                     x.shape[1], prologue, norm.data_ptr() if norm is not None else None, eps,
@@ -184,3 +186,26 @@ def test_gemm_row_pitch_not_16_bytes_falls_back_to_gemv():
     assert st == _lib.XM_ERR_UNSUPPORTED and b"multiple of 16" in _lib.lib.xm_last_error()
     yq = qlinear(W, x).cpu().numpy()
     assert rel_err(yq, x.float().cpu().numpy() @ w.T) < 1e-3
+
+
+@pytest.mark.parametrize("name,m,n,k", [("Q6_K", 64, 4096, 14336), ("Q4_K", 200, 4096, 4096),
+                                        ("Q8_0", 96, 1024, 2048), ("Q4_K", 37, 11008, 4096)])
+@pytest.mark.parametrize("accumulate", [False, True])
+def test_gemm_split_k(name, m, n, k, accumulate):
+    """Few output tiles: the GEMM cuts K into parts (partial planes in the workspace, then one ordered
+    reduction with the bias and the residual add).  Against the oracle, bit-identical on a second run,
+    and within summation-order distance of the unsplit GEMM."""
+    raw, w = wref(name, n, k, 111)
+    rng = np.random.default_rng(112)
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(113)).to(torch.bfloat16)
+    b = torch.from_numpy(rng.standard_normal(n).astype(np.float32)).cuda()
+    h0 = rng.standard_normal((m, n)).astype(np.float32) if accumulate else np.zeros((m, n), np.float32)
+    W = GGUFTensor(raw, name, (n, k))
+    ys = [_gemm(W, x.cuda(), y=torch.from_numpy(h0.copy()).cuda(), accumulate=accumulate, bias=b, split=True)
+          for _ in range(2)]
+    assert torch.equal(ys[0], ys[1])
+    y1 = _gemm(W, x.cuda(), y=torch.from_numpy(h0.copy()).cuda(), accumulate=accumulate, bias=b)
+    ref = h0 + x.float().numpy() @ w.T + b.cpu().numpy()
+    tol = 1e-5 * max(1.0, k / 4096)
+    assert rel_err(ys[0].cpu().numpy(), ref) < tol, rel_err(ys[0].cpu().numpy(), ref)
+    assert rel_err(ys[0].cpu().numpy(), y1.cpu().numpy()) < tol

@@ -41,6 +41,7 @@ SIGNATURES = {
     "xm_split_activation": (_int, [_vp, _int, _i64, _i64, _vp, _i64, _vp]),
     "xm_qgemv_presplit": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp]),
     "xm_qgemm_workspace_size": (_i64, [_i64, _i64]),
+    "xm_qgemm_workspace_size_n": (_i64, [_i64, _i64, _i64]),
     "xm_qgemm": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _int, _i64, _vp, _vp, _vp, _i64, _vp]),
     "xm_qgemm_ex": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _int, _i64, _i64, _int, _vp, _f32, _vp, _vp, _int,
                            _vp, _i64, _vp]),

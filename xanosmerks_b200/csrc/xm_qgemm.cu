@@ -100,6 +100,11 @@ XM_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+XM_DEV void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
 XM_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor: K-major operand in the 128-byte swizzle
@@ -1069,9 +1074,12 @@ constexpr int kTmMaxStages = 6;
 constexpr int kTmStageK = 128;              // K values per pipeline stage
 constexpr int kTmRows = 128;                // weight rows per CTA
 constexpr int kTmEpiBox = 32 * 32;          // fp32 output box: 32 tokens x 32 features
+constexpr double kTmDualStageClk = 1000.0;  // host cost model: one 128-K stage with two MMA threads
+
+constexpr int kTmMaxRaw = 6;                // raw record ring slots (256-wide K columns), as shared memory allows
 
 struct TmSmem {
-  uint64_t wfull[kMaxRawStages], wempty[kMaxRawStages];
+  uint64_t wfull[kTmMaxRaw], wempty[kTmMaxRaw];
   uint64_t ofull[kTmMaxStages], oempty[kTmMaxStages];
   uint64_t acc_full[2], acc_empty[2];
   uint64_t col_free[4];            // ping-pong mode: the epilogue has read these 64 columns of the last tile
@@ -1092,6 +1100,11 @@ XM_DEV void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "
 XM_DEV void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
                ::"l"(map), "r"(c0), "r"(c1), "r"(smem_u32(src))
+               : "memory");
+}
+XM_DEV void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
+               ::"l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src))
                : "memory");
 }
 XM_DEV void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
@@ -1137,6 +1150,29 @@ XM_DEV void tc2_mma_stage128(uint32_t d, uint32_t a, uint32_t blo, uint32_t bhi,
       "}"
       ::"r"(d), "r"(a), "r"(blo), "r"(bhi), "r"(bh), "r"(idesc), "r"(first), "r"(a + 8u), "r"(a + 16u),
         "r"(a + 24u), "r"(a + 32u), "r"(a + 40u), "r"(a + 48u), "r"(a + 56u)
+      : "memory");
+}
+
+// Half a stage (K steps 4h .. 4h + 3: one 64-K box) for the dual-issue mode:
+// A columns a + 8k, B descriptors {blo + 2k, bhi}.
+XM_DEV void tc2_mma_half64(uint32_t d, uint32_t a, uint32_t blo, uint32_t bhi, uint32_t idesc, uint32_t first) {
+  asm volatile(
+      "{\n"
+      " .reg .pred p0, p1;\n"
+      " .reg .b32 l;\n"
+      " .reg .b64 bd;\n"
+      " setp.eq.b32 p0, %5, 0;\n"
+      " setp.eq.b32 p1, %5, %5;\n"
+      " mov.b64 bd, {%2, %3};\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], bd, %4, p0;\n"
+      " add.u32 l, %2, 2;\n mov.b64 bd, {l, %3};\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], [%6], bd, %4, p1;\n"
+      " add.u32 l, %2, 4;\n mov.b64 bd, {l, %3};\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], [%7], bd, %4, p1;\n"
+      " add.u32 l, %2, 6;\n mov.b64 bd, {l, %3};\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], [%8], bd, %4, p1;\n"
+      "}"
+      ::"r"(d), "r"(a), "r"(blo), "r"(bhi), "r"(idesc), "r"(first), "r"(a + 8u), "r"(a + 16u), "r"(a + 24u)
       : "memory");
 }
 
@@ -1195,13 +1231,15 @@ XM_DEV bool tm_tile(const PairW<NMAP>& pw, int t, int M, int TM, int TW, int NT,
 // 64-127), so the epilogue warps of lane quarters q and q + 2 hold the gate
 // and up accumulators of the same features and combine them through shared
 // memory: y = act(gate) * up, 128 features per CTA pair.
-template <int T, int NMAP, bool GU>
+template <int T, int NMAP, bool GU, bool DUAL = false>
 __global__ void __launch_bounds__(kTmThreads, 1)
     k_qgemm_tm(const __grid_constant__ CUtensorMap map_b, const __grid_constant__ PairW<NMAP> pw,
-               const __grid_constant__ PairW<NMAP> pw3, const __grid_constant__ CUtensorMap map_y, int y_tma, int M,
-               int N, int K, int NT, int nacc, int S, int RW, int TM, const float* __restrict__ rowscale,
+               const __grid_constant__ PairW<NMAP> pw3, const __grid_constant__ CUtensorMap map_y, int y_tma,
+               const __grid_constant__ CUtensorMap map_p, int ksplit, float* __restrict__ part, int M, int N, int K,
+               int NT, int nacc, int S, int RW, int TM, const float* __restrict__ rowscale,
                const float* __restrict__ bias, float* __restrict__ y, int acc, int act) {
   using CG = ColGeom<T>;
+  constexpr bool dual = DUAL;
   constexpr int TWID = GU ? kTmRows : 2 * kTmRows;   // output features per tile
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1219,9 +1257,15 @@ __global__ void __launch_bounds__(kTmThreads, 1)
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int TW = (N + TWID - 1) / TWID;
   const int NTILES = TM * TW * (NMAP == 1 ? 1 : pw.groups);
-  const int KB = K >> 8, nks = K / kTmStageK;
+  const int KB = K >> 8;
+  // split-K: unit u = tile (u % NTILES) x K part (u / NTILES); part sp covers
+  // the 256-wide columns [kcol(sp), kcol(sp + 1)), an even number of them
+  const int NUNITS = NTILES * ksplit;
+  auto kcol = [&](int sp) { return ksplit == 1 ? (sp ? KB : 0) : 2 * ((KB >> 1) * sp / ksplit); };
   const bool pp = nacc == 0;                      // ping-pong accumulator (see above)
-  const uint32_t a_col0 = (uint32_t)(nacc * NT);  // first tensor-memory column of the A stages (nacc > 0)
+  constexpr int nd = dual ? 2 : 1;                // dual issue: two MMA threads, two partial accumulators per tile
+  const int accw = nd * NT;                       // tensor-memory columns of one tile's accumulator(s)
+  const uint32_t a_col0 = (uint32_t)(nacc * accw);   // first tensor-memory column of the A stages (nacc > 0)
 
   if (tid == 0) {
     for (int i = 0; i < RW; ++i) {
@@ -1230,10 +1274,10 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     }
     for (int i = 0; i < S; ++i) {
       mbar_init(&ctl->ofull[i], 2 + 2 * 8);       // rank 0 only: 2 producers + 8 decode warps per CTA
-      mbar_init(&ctl->oempty[i], 1);
+      mbar_init(&ctl->oempty[i], nd);             // one commit per MMA thread
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&ctl->acc_full[b], 1);
+      mbar_init(&ctl->acc_full[b], nd);
       mbar_init(&ctl->acc_empty[b], 2 * kPairEpiWarps);
     }
     for (int i = 0; i < 4; ++i) mbar_init(&ctl->col_free[i], kPairEpiWarps);   // this CTA's epilogue warps
@@ -1258,11 +1302,12 @@ __global__ void __launch_bounds__(kTmThreads, 1)
       grid_dep_wait();
       const uint32_t leader_ofull = mapa_shared(smem_u32(&ctl->ofull[0]), 0);
       uint32_t s = 0, ph = 0;
-      for (int t = pair; t < NTILES; t += npairs) {
+      for (int u = pair; u < NUNITS; u += npairs) {
+        const int t = u % NTILES, sp = u / NTILES;
         PairTile pt;
         if (!tm_tile(pw, t, M, TM, TW, NT, TWID, pt)) continue;
         const int bm = pt.am0 + (int)rank * (NT / 2);
-        for (int ks = 0; ks < nks; ++ks) {
+        for (int ks = 2 * kcol(sp); ks < 2 * kcol(sp + 1); ++ks) {
           pair_wait(&ctl->oempty[s], ph ^ 1);
           uint8_t* dst = sB + s * bstage;
           if (rank == 0) {
@@ -1278,27 +1323,37 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || (warp == 3 && dual)) {
     if (lane == 0 && rank == 0) {
-      // ---------------- MMA issuer ----------------
+      // ---------------- MMA issuer(s) ----------------
+      // Dual issue: warp 1 issues K steps 0-3 of every stage into the tile's
+      // first accumulator and warp 3 steps 4-7 into the second (the epilogue
+      // adds the two); each thread commits its own MMAs.
+      const uint32_t hsel = warp == 3 ? 1u : 0u;
       const uint32_t idesc = idesc_f16_f32_m256(NT);
       const uint64_t b0 = smem_desc_sw128(sB);
       const uint64_t bstep = (uint64_t)(bstage >> 4), bh = (uint64_t)(bhalf >> 4);
       uint32_t s = 0, ph = 0, it = 0;
-      for (int t = pair; t < NTILES; t += npairs) {
+      for (int un = pair; un < NUNITS; un += npairs) {
+        const int t = un % NTILES, sp = un / NTILES;
         PairTile pt;
         if (!tm_tile(pw, t, M, TM, TW, NT, TWID, pt)) continue;
         const uint32_t b = nacc != 1 ? (it & 1) : 0u, u = nacc != 1 ? (it >> 1) : it;
         if (!pp) pair_wait(&ctl->acc_empty[b], (u & 1) ^ 1);   // (ping-pong: the decode warps' col_free waits)
         tc_fence_after();
-        const uint32_t d = pp ? tmem + (it & 1u) * 256u : tmem + b * (uint32_t)NT;
+        const uint32_t d = pp ? tmem + (it & 1u) * 256u : tmem + b * (uint32_t)accw + hsel * (uint32_t)NT;
         const uint32_t abase = pp ? tmem + ((it & 1u) ^ 1u) * 256u : tmem + a_col0;
-        for (int ks = 0; ks < nks; ++ks) {
+        const int ks0 = 2 * kcol(sp), ks1 = 2 * kcol(sp + 1);
+        for (int ks = ks0; ks < ks1; ++ks) {
           pair_wait(&ctl->ofull[s], ph);
           tc_fence_after();
           const uint64_t bs = b0 + s * bstep;
-          tc2_mma_stage128(d, abase + s * 64u, (uint32_t)bs, (uint32_t)(bs >> 32), (uint32_t)bh, idesc,
-                           ks == 0 ? 1u : 0u);
+          if constexpr (dual)
+            tc2_mma_half64(d, abase + s * 64u + hsel * 32u, (uint32_t)bs + hsel * (uint32_t)bh, (uint32_t)(bs >> 32),
+                           idesc, ks == ks0 ? 1u : 0u);
+          else
+            tc2_mma_stage128(d, abase + s * 64u, (uint32_t)bs, (uint32_t)(bs >> 32), (uint32_t)bh, idesc,
+                             ks == ks0 ? 1u : 0u);
           tc2_commit_pair(&ctl->oempty[s]);      // both CTAs may refill the stage once these MMAs are done
           if (++s == (uint32_t)S) { s = 0; ph ^= 1; }
         }
@@ -1310,13 +1365,14 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     // ---------------- TMA producer: raw weight records ----------------
     if (lane == 0) {
       uint32_t rs = 0, rph = 0;
-      for (int t = pair; t < NTILES; t += npairs) {
+      for (int u = pair; u < NUNITS; u += npairs) {
+        const int t = u % NTILES, sp = u / NTILES;
         PairTile pt;
         if (!tm_tile(pw, t, M, TM, TW, NT, TWID, pt)) continue;
         const CUtensorMap* wmap = &pw.map[NMAP == 1 ? 0 : pt.g];
         const CUtensorMap* wmap3 = &pw3.map[NMAP == 1 ? 0 : pt.g];
         const int wn = pt.col0 + (GU ? (int)rank * (kTmRows / 2) : (int)rank * kTmRows);
-        for (int kb = 0; kb < KB; ++kb) {
+        for (int kb = kcol(sp); kb < kcol(sp + 1); ++kb) {
           pair_wait(&ctl->wempty[rs], rph ^ 1);
           mbar_arrive_expect_tx(&ctl->wfull[rs], (uint32_t)wstage);
           const int wx = ((kb * CG::CB) & ~15) >> 1;   // 16-byte aligned start, in 16-bit elements
@@ -1337,18 +1393,20 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     const uint32_t lane0 = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(hs * 32);
     uint32_t s = (uint32_t)grp, ph = 0, rs = 0, rph = 0;   // this group's first stage is q = grp (< S)
     uint32_t it = 0;
-    for (int t = pair; t < NTILES; t += npairs) {
+    for (int u = pair; u < NUNITS; u += npairs) {
+      const int t = u % NTILES, sp = u / NTILES;
       PairTile pt;
       if (!tm_tile(pw, t, M, TM, TW, NT, TWID, pt)) continue;
       const uint32_t lane_addr = lane0 + (pp ? ((it & 1u) ^ 1u) * 256u : a_col0);
-      for (int kb = 0; kb < KB; ++kb) {
+      const int kb0 = kcol(sp);
+      for (int kb = kb0; kb < kcol(sp + 1); ++kb) {
         pair_wait(&ctl->wfull[rs], rph);
         const int mis = (kb * CG::CB) & 15;       // the column's offset in its staged box (0 for Q4_K)
         const uint8_t* rec = sW + rs * wstage + row * CG::BB + mis;
         pair_wait(&ctl->oempty[s], ph ^ 1);       // the MMAs that read these columns are done
         // ping-pong: the first write of a slot in a tile also waits for the
         // epilogue of the previous tile to have read these columns
-        if (pp && it > 0 && kb < 2) pair_wait(&ctl->col_free[s], (it - 1u) & 1u);
+        if (pp && it > 0 && kb - kb0 < 2) pair_wait(&ctl->col_free[s], (it - 1u) & 1u);
         tc_fence_after();
         uint32_t hv[16];
         item_regs<T>(rec, j, 0, hv);
@@ -1386,11 +1444,16 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     uint32_t nb = 0;
     const uint32_t leader_acc_empty = mapa_shared(smem_u32(&ctl->acc_empty[0]), 0);
     uint32_t it = 0;
-    for (int t = pair; t < NTILES; t += npairs) {
+    for (int un = pair; un < NUNITS; un += npairs) {
+      const int t = un % NTILES, sp = un / NTILES;
       PairTile pt;
       if (!tm_tile(pw, t, M, TM, TW, NT, TWID, pt)) continue;
       const uint32_t b = nacc != 1 ? (it & 1) : 0u, u = nacc != 1 ? (it >> 1) : it;
-      const uint32_t dcol = pp ? (it & 1u) * 256u : b * (uint32_t)NT;
+      // a K part's partial sums go to part[sp] (row-scaled; the bias and the
+      // residual add come in the ordered reduction)
+      float* const ydst = ksplit > 1 ? part + (int64_t)sp * M * N : y;
+      const int uacc = ksplit > 1 ? 0 : acc;
+      const uint32_t dcol = pp ? (it & 1u) * 256u : b * (uint32_t)accw;
       uint32_t rel = 0;                           // ping-pong: 64-column slots released so far
       const int f0 = pt.col0 + (GU ? (int)rank * (kTmRows / 2) + (quarter & 1) * 32 : (int)rank * kTmRows + quarter * 32);
       const int f = f0 + lane;                    // this thread's output feature
@@ -1404,7 +1467,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         const int tok = pt.am0 + ch * 32 + lane;
         rsv[ch] = (ch < nch && tok < pt.mhi) ? rowscale[tok] : 0.f;
       }
-      const float bv = (bias && fok) ? bias[f] : 0.f;
+      const float bv = (bias && fok && ksplit == 1) ? bias[f] : 0.f;
       pair_wait(&ctl->acc_full[b], u & 1);
       tc_fence_after();
 #pragma unroll
@@ -1412,7 +1475,19 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         const int tok0 = pt.am0 + ch * 32;
         if (ch >= nch || tok0 >= pt.mhi) break;
         uint32_t v[32];
-        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + dcol + (uint32_t)(ch * 32), v);
+        const uint32_t tq = tmem + ((uint32_t)(quarter * 32) << 16) + dcol + (uint32_t)(ch * 32);
+        tmem_ld32(tq, v);
+        if constexpr (dual) {                     // add the second issuer's partial sums
+#pragma unroll
+          for (int hh = 0; hh < 4; ++hh) {
+            uint32_t w2[8];
+            tmem_ld8(tq + (uint32_t)NT + (uint32_t)(hh * 8), w2);
+            tmem_ld_wait();
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+              v[hh * 8 + c] = __float_as_uint(__uint_as_float(v[hh * 8 + c]) + __uint_as_float(w2[c]));
+          }
+        }
         tmem_ld_wait();
         if (pp && (ch & 1)) {                     // chunks 2s, 2s + 1 read: slot s may take A of the next tile
           tc_fence_before();
@@ -1468,7 +1543,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
           continue;
         }
         const float vs = rs;
-        if (y_tma && (NMAP == 1 || tok0 + 32 <= pt.mhi)) {
+        if ((ksplit > 1 || y_tma) && (NMAP == 1 || tok0 + 32 <= pt.mhi)) {
           float* box = box0 + nb * kTmEpiBox;
           if (lane == 0) bulk_wait_read1();       // the store issued from this box two chunks ago has read it
           __syncwarp();
@@ -1477,7 +1552,9 @@ __global__ void __launch_bounds__(kTmThreads, 1)
           fence_proxy_async_smem();               // generic-proxy writes -> visible to the bulk copy
           __syncwarp();
           if (lane == 0) {
-            if (acc)
+            if (ksplit > 1)
+              tma_store_3d(&map_p, box, f0, tok0, sp);
+            else if (acc)
               tma_reduce_add_2d(&map_y, box, f0, tok0);
             else
               tma_store_2d(&map_y, box, f0, tok0);
@@ -1490,8 +1567,8 @@ __global__ void __launch_bounds__(kTmThreads, 1)
             const float o = __uint_as_float(v[c]) * __shfl_sync(~0u, vs, c) + bv;
             const int tok = tok0 + c;
             if (tok < pt.mhi && fok) {
-              float* yp = y + (int64_t)tok * N + f;
-              if (acc)
+              float* yp = ydst + (int64_t)tok * N + f;
+              if (uacc)
                 *yp += o;
               else
                 *yp = o;
@@ -1821,8 +1898,63 @@ int launch_pair_grouped(const CUtensorMap& map_a, const uint8_t* const* h_w, con
 }
 
 // ---- tensor-memory-A kernel ----
+constexpr int kTmMaxSplit = 4;              // K parts at most (dense GEMM)
+
+// Partial planes of a split-K launch, [ks][rows][n] fp32, as a 3-D tensor
+// map with 32 x 32 x 1 boxes, so that a box is clipped at the end of its own
+// plane's rows.
+bool encode_part_map(CUtensorMap* map, const float* part, int64_t rows, int64_t n, int ks) {
+  if ((n * 4) % 16 || ((uintptr_t)part & 15)) return false;
+  EncodeTiledFn encode = get_encode();
+  if (!encode) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)n, (cuuint64_t)rows, (cuuint64_t)ks};
+  const cuuint64_t strides[2] = {(cuuint64_t)n * 4, (cuuint64_t)(rows * n * 4)};
+  const cuuint32_t box[3] = {32, 32, 1};
+  const cuuint32_t es[3] = {1, 1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(part), dims, strides, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Ordered reduction of the K parts: y = [y +] ((part[0] + part[1] + ...) +
+// bias), the same association as the unsplit epilogue (y [+]= acc + bias)
+// with the accumulator summed part by part; n % 4 == 0.
+__global__ void __launch_bounds__(256) k_splitk_reduce(const float* __restrict__ part, int ks, int64_t mn, int n,
+                                                       const float* __restrict__ bias, float* __restrict__ y,
+                                                       int acc) {
+  const int64_t n4 = mn >> 2;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 s = __ldcs(reinterpret_cast<const float4*>(part) + i);
+    for (int p = 1; p < ks; ++p) {
+      const float4 v = __ldcs(reinterpret_cast<const float4*>(part + (int64_t)p * mn) + i);
+      s.x += v.x;
+      s.y += v.y;
+      s.z += v.z;
+      s.w += v.w;
+    }
+    if (bias) {
+      const int f = (int)((i * 4) % n);
+      const float4 b = *reinterpret_cast<const float4*>(bias + f);
+      s.x += b.x;
+      s.y += b.y;
+      s.z += b.z;
+      s.w += b.w;
+    }
+    float4* yp = reinterpret_cast<float4*>(y) + i;
+    if (acc) {
+      const float4 o = *yp;
+      s.x = o.x + s.x;
+      s.y = o.y + s.y;
+      s.z = o.z + s.z;
+      s.w = o.w + s.w;
+    }
+    *yp = s;
+  }
+}
+
 struct TmCfg {
-  int NT, nacc, S, RW, smem;
+  int NT, nacc, S, RW, smem, dual;
+  int ks = 1;                      // K parts (split-K units per output tile)
 };
 
 int tm_smem_bytes(int NT, int S, int RW, int BB, bool gu = false) {
@@ -1848,47 +1980,76 @@ bool encode_y_map(CUtensorMap* map, const float* y, int64_t rows, int64_t n) {
 // Token-tile options: NT a multiple of 32 (<= 256); two accumulators where
 // they fit beside 4 A stages (so the epilogue of one tile overlaps the next
 // tile's main loop), then as many A stages (<= 6) as tensor and shared memory
-// hold.  S = 0 if fewer than 3 stages fit.
-TmCfg tm_stages(int NT, int BB, bool gu = false, bool pp_ok = false) {
-  const int nacc = 2 * NT + 4 * 64 <= 512 ? 2 : 1;
+// hold, then as many raw record slots (2 .. kTmMaxRaw) as the rest of shared
+// memory holds: the record ring is what keeps a pair fed when the MMAs of a
+// stage are short (narrow tiles), since each slot waits one HBM round trip.
+// S = 0 if fewer than 3 stages fit.  Dual issue doubles a tile's accumulator
+// columns (two partial sums of NT columns) and has no ping-pong form.
+TmCfg tm_stages(int NT, int BB, bool gu = false, bool pp_ok = false, bool dual = false) {
+  const int accw = dual ? 2 * NT : NT;
+  const int nacc = 2 * accw + 4 * 64 <= 512 ? 2 : 1;
+  auto raw_slots = [&](int S) {
+    int RW = kPairRaw;
+    while (RW < kTmMaxRaw && tm_smem_bytes(NT, S, RW + 1, BB, gu) <= 227 * 1024) ++RW;
+    return RW;
+  };
   // one accumulator: ping-pong halves when 4 stages fit (nacc = 0)
-  if (nacc == 1 && pp_ok && tm_smem_bytes(NT, 4, kPairRaw, BB, gu) <= 227 * 1024)
-    return {NT, 0, 4, kPairRaw, tm_smem_bytes(NT, 4, kPairRaw, BB, gu)};
-  int S = std::min(kTmMaxStages, (512 - nacc * NT) / 64);
+  if (!dual && nacc == 1 && pp_ok && tm_smem_bytes(NT, 4, kPairRaw, BB, gu) <= 227 * 1024) {
+    const int RW = raw_slots(4);
+    return {NT, 0, 4, RW, tm_smem_bytes(NT, 4, RW, BB, gu), 0, 1};
+  }
+  int S = std::min(kTmMaxStages, (512 - nacc * accw) / 64);
   while (S >= 3 && tm_smem_bytes(NT, S, kPairRaw, BB, gu) > 227 * 1024) --S;
   if (S < 3) S = 0;
-  return {NT, nacc, S, kPairRaw, tm_smem_bytes(NT, S, kPairRaw, BB, gu)};
+  const int RW = S ? raw_slots(S) : kPairRaw;
+  return {NT, nacc, S, RW, tm_smem_bytes(NT, S, RW, BB, gu), dual ? 1 : 0, 1};
 }
 
-template <int T, int NMAP, bool GU = false>
+template <int T, int NMAP, bool GU = false, bool DUAL = false>
 const void* tm_kernel() {
-  return reinterpret_cast<const void*>(k_qgemm_tm<T, NMAP, GU>);
+  return reinterpret_cast<const void*>(k_qgemm_tm<T, NMAP, GU, DUAL>);
 }
 
 // Token tile for m rows (per group) and n output features: estimated clocks
 // per pair = rounds x (main loop + the epilogues that do not overlap it).  A
-// 128-K stage costs the larger of its MMA time (4 NT clocks) and the issuing
-// thread's cost (8 MMA issues and a barrier wait beside 16 decode warps,
-// ~1120 clocks measured); the epilogue ~1400 + 20 NT clocks, hidden behind
-// the next tile except with one non-ping-pong accumulator.
-TmCfg choose_tm(int64_t m, int64_t groups, int64_t n, int64_t k, int pairs, int BB, bool gu = false) {
-  TmCfg best{0, 0, 0, 0, 0};
+// 128-K stage costs the larger of its MMA time (4 NT clocks) and the decode
+// of 128 rows x 128 K beside it (~1000-1120 clocks measured, the MMA thread's
+// issue included; ~1000 with two MMA threads); the epilogue ~1400 + 20 NT
+// clocks (+ 10 NT for the second partial sum), hidden behind the next tile
+// except with one non-ping-pong accumulator.  K parts (ks > 1, at most
+// max_ks, dense only) cut each tile's K loop into ks units so that more pairs
+// work when the tiles are few: each unit pays a pipeline fill (~4000 clocks)
+// and an epilogue, and the ordered reduction reads the ks partial planes
+// (~2600 bytes per clock) after a launch (~6000 clocks).
+TmCfg choose_tm(int64_t m, int64_t groups, int64_t n, int64_t k, int pairs, int BB, bool gu = false,
+                bool dual_ok = false, int max_ks = 1) {
+  TmCfg best{0, 0, 0, 0, 0, 0, 1};
   double best_t = 1e30;
-  const double nks = (double)(k / kTmStageK);
+  const int64_t kcols = k / 256;
   const bool pp_ok = (k / kTmStageK) % 4 == 0;
   const int64_t tw = gu ? (n + kTmRows - 1) / kTmRows : (n + 255) / 256;
   for (int nt = 256; nt >= 32; nt -= 32) {
     if (nt > 32 && nt - 32 >= m) continue;      // a smaller tile already holds every row
-    const TmCfg c = tm_stages(nt, BB, gu, pp_ok);
-    if (c.S < 3) continue;
-    const int64_t tiles = groups * tw * ((m + nt - 1) / nt);
-    const double rounds = (double)((tiles + pairs - 1) / pairs);
-    const double main_clk = nks * std::max(1120.0, 4.0 * nt + 90.0);
-    const double epi_clk = 1400.0 + 20.0 * nt;
-    const double t = rounds * main_clk + (c.nacc == 1 ? rounds : 1.0) * epi_clk;
-    if (t < best_t) {
-      best_t = t;
-      best = c;
+    for (int dual = 0; dual < (dual_ok ? 2 : 1); ++dual) {
+      const TmCfg c = tm_stages(nt, BB, gu, pp_ok, dual != 0);
+      if (c.S < 3) continue;
+      const int64_t tiles = groups * tw * ((m + nt - 1) / nt);
+      for (int ks = 1; ks <= max_ks; ++ks) {
+        if (ks > 1 && (kcols % 2 || ks > kcols / 2)) break;
+        const int64_t units = tiles * ks;
+        const double rounds = (double)((units + pairs - 1) / pairs);
+        const double stages = 2.0 * (ks == 1 ? (double)kcols : 2.0 * (double)((kcols / 2 + ks - 1) / ks));
+        const double main_clk = stages * std::max(dual ? kTmDualStageClk : 1120.0, 4.0 * nt + 90.0) +
+                                (ks > 1 ? 4000.0 : 0.0);
+        const double epi_clk = 1400.0 + (dual ? 30.0 : 20.0) * nt;
+        double t = rounds * main_clk + (c.nacc == 1 ? rounds : 1.0) * epi_clk;
+        if (ks > 1) t += 6000.0 + (double)(ks + 2) * (double)(m * n) * 4.0 / 2600.0;
+        if (t < best_t * 0.97 || (t < best_t && ks == 1)) {   // a split must win clearly
+          best_t = t;
+          best = c;
+          best.ks = ks;
+        }
+      }
     }
   }
   return best;
@@ -1897,8 +2058,10 @@ TmCfg choose_tm(int64_t m, int64_t groups, int64_t n, int64_t k, int pairs, int 
 template <int T, int NMAP, bool GU = false>
 int launch_tm(const CUtensorMap& map_b, const PairW<NMAP>& pw, const PairW<NMAP>& pw3, int64_t m, int64_t n,
               int64_t k, int tm, const TmCfg& cfg, int pairs, const float* rowscale, const float* bias, float* y,
-              int acc, int act, cudaStream_t st) {
+              int acc, int act, cudaStream_t st, const CUtensorMap* map_p = nullptr, float* part = nullptr) {
   const void* fn = tm_kernel<T, NMAP, GU>();
+  if constexpr (NMAP == 1 && !GU)
+    if (cfg.dual) fn = tm_kernel<T, 1, false, true>();
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, cfg.smem);
   if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemm: smem attribute: %s", cudaGetErrorString(e));
   cudaLaunchConfig_t lc = {};
@@ -1918,8 +2081,23 @@ int launch_tm(const CUtensorMap& map_b, const PairW<NMAP>& pw, const PairW<NMAP>
   CUtensorMap map_y;
   memset(&map_y, 0, sizeof(map_y));
   const int y_tma = encode_y_map(&map_y, y, m, n) ? 1 : 0;
-  e = cudaLaunchKernelEx(&lc, k_qgemm_tm<T, NMAP, GU>, map_b, pw, pw3, map_y, y_tma, (int)m, (int)n, (int)k,
-                         cfg.NT, cfg.nacc, cfg.S, cfg.RW, tm, rowscale, bias, y, acc, act);
+  CUtensorMap mp;
+  if (map_p)
+    mp = *map_p;
+  else
+    memset(&mp, 0, sizeof(mp));
+  const int ksplit = map_p ? cfg.ks : 1;
+  if constexpr (NMAP == 1 && !GU) {
+    if (cfg.dual)
+      e = cudaLaunchKernelEx(&lc, k_qgemm_tm<T, 1, false, true>, map_b, pw, pw3, map_y, y_tma, mp, ksplit, part,
+                             (int)m, (int)n, (int)k, cfg.NT, cfg.nacc, cfg.S, cfg.RW, tm, rowscale, bias, y, acc, act);
+    else
+      e = cudaLaunchKernelEx(&lc, k_qgemm_tm<T, 1, false, false>, map_b, pw, pw3, map_y, y_tma, mp, ksplit, part,
+                             (int)m, (int)n, (int)k, cfg.NT, cfg.nacc, cfg.S, cfg.RW, tm, rowscale, bias, y, acc, act);
+  } else {
+    e = cudaLaunchKernelEx(&lc, k_qgemm_tm<T, NMAP, GU>, map_b, pw, pw3, map_y, y_tma, mp, 1, (float*)nullptr,
+                           (int)m, (int)n, (int)k, cfg.NT, cfg.nacc, cfg.S, cfg.RW, tm, rowscale, bias, y, acc, act);
+  }
   if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "qgemm tm launch: %s", cudaGetErrorString(e));
   return xm_check_launch("qgemm tm");
 }
@@ -1928,13 +2106,18 @@ int launch_tm(const CUtensorMap& map_b, const PairW<NMAP>& pw, const PairW<NMAP>
 // device cannot hold it.
 template <int T>
 int launch_tm_gemm(const __half* a16, const uint8_t* w, int64_t m, int64_t n, int64_t k, const float* rowscale,
-                   const float* bias, float* y, int acc, cudaStream_t st) {
+                   const float* bias, float* y, int acc, cudaStream_t st, float* part = nullptr,
+                   int64_t part_bytes = 0) {
   constexpr int BB = ColGeom<T>::BB;
   const void* fn = tm_kernel<T, 1>();
   const TmCfg probe = tm_stages(128, BB);
   const int cap = cluster_capacity(fn, kTmThreads, probe.smem);
   if (cap < 1) return 1;
-  const TmCfg cfg = choose_tm(m, 1, n, k, cap, BB);
+  // K parts need room for their partial planes and 16-byte output rows
+  int max_ks = 1;
+  if (part && n % 4 == 0 && !((uintptr_t)y & 15) && !((uintptr_t)bias & 15))
+    while (max_ks < kTmMaxSplit && (int64_t)(max_ks + 1) * m * n * 4 <= part_bytes) ++max_ks;
+  const TmCfg cfg = choose_tm(m, 1, n, k, cap, BB, false, true, max_ks);
   if (cfg.S < 3) return 1;
   const int cap_cfg = cluster_capacity(fn, kTmThreads, cfg.smem);
   if (cap_cfg < 1) return 1;
@@ -1947,8 +2130,18 @@ int launch_tm_gemm(const __half* a16, const uint8_t* w, int64_t m, int64_t n, in
   pw.groups = 1;
   const int64_t tm = (m + cfg.NT - 1) / cfg.NT;
   const int64_t tiles = tm * ((n + 255) / 256);
-  const int pairs = (int)std::min<int64_t>(tiles, cap_cfg);
-  return launch_tm<T, 1>(map_b, pw, pw, m, n, k, (int)tm, cfg, pairs, rowscale, bias, y, acc, 0, st);
+  const int pairs = (int)std::min<int64_t>(tiles * cfg.ks, cap_cfg);
+  if (cfg.ks == 1) return launch_tm<T, 1>(map_b, pw, pw, m, n, k, (int)tm, cfg, pairs, rowscale, bias, y, acc, 0, st);
+  CUtensorMap map_p;
+  if (!encode_part_map(&map_p, part, m, n, cfg.ks))
+    return launch_tm<T, 1>(map_b, pw, pw, m, n, k, (int)tm, TmCfg{cfg.NT, cfg.nacc, cfg.S, cfg.RW, cfg.smem, cfg.dual, 1},
+                           (int)std::min<int64_t>(tiles, cap_cfg), rowscale, bias, y, acc, 0, st);
+  rc = launch_tm<T, 1>(map_b, pw, pw, m, n, k, (int)tm, cfg, pairs, rowscale, bias, y, acc, 0, st, &map_p, part);
+  if (rc) return rc;
+  const int64_t mn4 = m * n / 4;
+  const unsigned rgrid = (unsigned)std::min<int64_t>((mn4 + 255) / 256, 148 * 8);
+  k_splitk_reduce<<<rgrid, 256, 0, st>>>(part, cfg.ks, m * n, (int)n, bias, y, acc);
+  return xm_check_launch("qgemm split-K reduction");
 }
 
 template <int T>
@@ -2023,11 +2216,13 @@ struct PairDense {
   int acc;
   cudaStream_t st;
   const __half* a16;
+  float* part;                     // split-K partial planes (workspace beyond the activation), or null
+  int64_t part_bytes;
   int rc = 1;
   template <int T>
   void operator()() {
     // tensor-memory-A kernel; the CTA-pair kernel where the device cannot hold it
-    rc = launch_tm_gemm<T>(a16, w, m, n, k, rowscale, bias, y, acc, st);
+    rc = launch_tm_gemm<T>(a16, w, m, n, k, rowscale, bias, y, acc, st, part, part_bytes);
     if (rc == 1) rc = launch_pair_gemm<T>(*map_a, w, m, n, k, rowscale, bias, y, acc, st);
   }
 };
@@ -2138,6 +2333,20 @@ extern "C" int64_t xm_qgemm_workspace_size(int64_t m, int64_t k) {
 }
 
 namespace {
+// the split-K partial planes start after the activation and its row scales
+int64_t qgemm_part_offset(int64_t m, int64_t k) {
+  return ((m * k * 2 + 255) / 256) * 256 + ((m * 4 + 255) / 256) * 256;
+}
+constexpr int64_t kSplitMaxMN = int64_t(1) << 23;   // split-K only for outputs of at most 8M elements
+}  // namespace
+
+extern "C" int64_t xm_qgemm_workspace_size_n(int64_t m, int64_t n, int64_t k) {
+  if (m <= 0 || k <= 0 || n <= 0) return 0;
+  if (m * n > kSplitMaxMN) return xm_qgemm_workspace_size(m, k);
+  return qgemm_part_offset(m, k) + (int64_t)kTmMaxSplit * m * n * 4;
+}
+
+namespace {
 template <typename XT>
 void launch_prep(const void* x, int prologue, int64_t m, int64_t k, int64_t ldx, const float* norm_w, float eps,
                  __half* x16, float* rowscale, cudaStream_t st) {
@@ -2202,7 +2411,14 @@ extern "C" int xm_qgemm_ex(int qtype, const void* d_w, int64_t w_bytes, int64_t 
   CUtensorMap map_a;
   rc = encode_a16(&map_a, x16, m, k);
   if (rc) return rc;
-  PairDense pd{&map_a, (const uint8_t*)d_w, m, n, k, rowscale, d_bias, d_y, accumulate ? 1 : 0, st, x16};
+  float* part = nullptr;
+  int64_t part_bytes = 0;
+  if (m * n <= kSplitMaxMN && workspace_bytes > qgemm_part_offset(m, k)) {
+    part = (float*)((uint8_t*)d_workspace + qgemm_part_offset(m, k));
+    part_bytes = workspace_bytes - qgemm_part_offset(m, k);
+  }
+  PairDense pd{&map_a, (const uint8_t*)d_w, m, n, k, rowscale, d_bias, d_y, accumulate ? 1 : 0, st, x16, part,
+               part_bytes};
   dispatch_quant(qtype, pd);
   if (pd.rc != 1) return pd.rc;
   if (qtype != T_Q4_K)

@@ -383,7 +383,7 @@ class LlamaDecoder:
         if not gemm_supported(wt.qtype, k):
             self._gemv(wt, x, rows, y, prologue, norm, accumulate)
             return
-        need = lib.xm_qgemm_workspace_size(rows, k)
+        need = lib.xm_qgemm_workspace_size_n(rows, n, k)
         if self._gemm_ws is None or self._gemm_ws.numel() < need:
             self._gemm_ws = torch.empty(need, dtype=torch.uint8, device=self.dev)
         check(lib.xm_qgemm_ex(wt.qtype.type_id, wt.data.data_ptr(), wt.nbytes, n, k, x.data_ptr(), DT_F32, rows,

@@ -123,7 +123,7 @@ def _qmatmul(weight: GGUFTensor, x2: torch.Tensor, y: torch.Tensor, b, prologue:
         return
     gemm = gemm_supported(qt, k)
     if (m > 8 and gemm) or (m <= 8 and prologue != PRO_NONE and qt.name not in _PROLOGUE_GEMV_TYPES and gemm):
-        ws = _workspace(dev, stream, lib.xm_qgemm_workspace_size(m, k))
+        ws = _workspace(dev, stream, lib.xm_qgemm_workspace_size_n(m, n, k))
         check(lib.xm_qgemm_ex(qt.type_id, weight.data.data_ptr(), weight.nbytes, n, k, x2.data_ptr(), dt, m, kin,
                               prologue, _ptr(nw), eps, _ptr(b), y.data_ptr(), 0, ws.data_ptr(), ws.numel(), st),
               "qgemm")
