@@ -1,11 +1,11 @@
 """Concurrent calls on two CUDA streams: each (device, stream) has its own scratch workspace
-(activation split, fp16 activation and row scales), so GEMV and GEMM calls running at the same
+(activation split, fp16 activation and row scales, split-K partial planes), so GEMV and GEMM calls running at the same
 time on different streams give the same bits as the same calls on one stream."""
 
-import numpy as np
 import pytest
 import torch
 
+from tests.helpers import rel_err
 from xanosmerks_b200.ops import GGUFTensor, qlinear
 from xanosmerks_b200.synth import make_weight
 
@@ -46,4 +46,5 @@ def test_qlinear_two_streams_match_one_stream():
         y4 = qlinear(w2, xs[1])
     torch.cuda.synchronize()
     assert torch.equal(y4, ref[1][1])
-    assert np.allclose(yb[:300].cpu().numpy(), qlinear(w1, big[:300]).cpu().numpy(), rtol=0, atol=1e-3)
+    # 300 rows of 4096 x 4096 take the split-K path, 2048 rows do not: only the summation order differs
+    assert rel_err(yb[:300].cpu().numpy(), qlinear(w1, big[:300]).cpu().numpy()) < 1e-5

@@ -1403,16 +1403,18 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         pair_wait(&ctl->wfull[rs], rph);
         const int mis = (kb * CG::CB) & 15;       // the column's offset in its staged box (0 for Q4_K)
         const uint8_t* rec = sW + rs * wstage + row * CG::BB + mis;
+        // decode both 32-weight items first (one pass over the record bytes),
+        // then wait for the tensor-memory columns
+        uint32_t hv[16], hv1[16];
+        item_regs<T>(rec, j, 0, hv);
+        item_regs<T>(rec, j, 1, hv1);
         pair_wait(&ctl->oempty[s], ph ^ 1);       // the MMAs that read these columns are done
         // ping-pong: the first write of a slot in a tile also waits for the
         // epilogue of the previous tile to have read these columns
         if (pp && it > 0 && kb - kb0 < 2) pair_wait(&ctl->col_free[s], (it - 1u) & 1u);
         tc_fence_after();
-        uint32_t hv[16];
-        item_regs<T>(rec, j, 0, hv);
         tmem_st16(lane_addr + s * 64u, hv);
-        item_regs<T>(rec, j, 1, hv);
-        tmem_st16(lane_addr + s * 64u + 16u, hv);
+        tmem_st16(lane_addr + s * 64u + 16u, hv1);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
