@@ -2,10 +2,12 @@
 GQA attention, O GEMV with residual, fused-norm gate/up GEMV, SwiGLU down GEMV
 with residual, output head, argmax) against the numpy oracle of the reference's
 TransformerModel forward with a KV cache, on the same GGUF weights.  Prompts
-of more than 8 tokens prefill on the tensor-core GEMM over all rows with the
-attention in chunks of up to 64 tokens (the 100-token case takes two chunks);
-shorter ones take the decode path 8 tokens at a time.  Decode steps run
-eagerly and from a captured CUDA graph."""
+of more than 8 tokens prefill on the tensor-core GEMM over all rows (16 or
+more tokens: one tensor-core attention call per layer for all sequences;
+9-15: the decode attention per 64-token chunk); shorter ones take the decode
+path 8 tokens at a time.  Decode steps run eagerly and from a captured CUDA
+graph; with 4 or more rows per step (batch 8) the Q6_K down projection and
+output head run on the tcgen05 GEMM instead of the GEMV."""
 
 import numpy as np
 import pytest
@@ -35,7 +37,8 @@ def oracle_weights(full):
             "lm_head": _f32(full["output"])}
 
 
-@pytest.mark.parametrize("batch,layers,prompt", [(1, 2, 11), (3, 1, 9), (2, 1, 5), (1, 1, 100), (2, 1, 70)])
+@pytest.mark.parametrize("batch,layers,prompt", [(1, 2, 11), (3, 1, 9), (2, 1, 5), (1, 1, 100), (2, 1, 70),
+                                                  (8, 1, 20), (4, 2, 6)])
 def test_decoder_matches_oracle(batch, layers, prompt):
     cfg = LlamaConfig(num_layers=layers, vocab_size=4096)
     full = synth_llama_weights(cfg, seed=7, device="cuda")

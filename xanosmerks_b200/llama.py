@@ -224,6 +224,14 @@ class LlamaDecoder:
         self.length = 0
         self.comm = None
         self._gemm_ws = None
+        # decode-step GEMMs (4+ rows) get a workspace of their own, allocated once: a captured step
+        # keeps its pointer, and the prefill's workspace may be replaced when a longer prompt comes
+        dec_need = 16
+        for wt in list(self.w.layers[0].values()) + [self.w.output]:
+            if isinstance(wt, GGUFTensor) and len(wt.shape) == 2:
+                r = self.B if wt is self.w.output else rows
+                dec_need = max(dec_need, lib.xm_qgemm_workspace_size_n(r, wt.shape[0], wt.shape[1]))
+        self.dec_gemm_ws = torch.zeros(dec_need, dtype=torch.uint8, device=dev)
         if collective not in ("p2p", "nccl"):
             raise ValueError(f"collective must be 'p2p' or 'nccl', got {collective!r}")
         self.collective = collective
@@ -291,29 +299,35 @@ class LlamaDecoder:
         st = self._stream()
         for li, lw in enumerate(self.w.layers):
             # attention block (forward.py:107-111)
-            self._gemv(lw["qkv"], self.h, rows, self.qkv, PRO_RMSNORM, lw["attn_norm"])
+            self._proj(lw["qkv"], self.h, rows, self.qkv, PRO_RMSNORM, lw["attn_norm"])
             check(lib.xm_attention(self.qkv.data_ptr(), self.qkv_dim, self.kc[li].data_ptr(),
                                    self.vc[li].data_ptr(), self.pos0.data_ptr(), B, lq, self.hq, self.hk,
                                    cfg.head_dim, cfg.rope_theta, self.max_ctx, self.attn.data_ptr(),
                                    self.hq * cfg.head_dim, self.attn_ws.data_ptr(), self.attn_ws.numel(), st),
                   "attention")
             if self.world == 1:
-                self._gemv(lw["o"], self.attn, rows, self.h, accumulate=True)
+                self._proj(lw["o"], self.attn, rows, self.h, accumulate=True)
             else:
-                self._gemv(lw["o"], self.attn, rows, self.part)
+                self._proj(lw["o"], self.attn, rows, self.part)
                 self._allreduce_add(rows)
             # MLP block (forward.py:113-116)
-            self._gemv(lw["gate_up"], self.h, rows, self.gu, PRO_RMSNORM, lw["ffn_norm"])
+            self._proj(lw["gate_up"], self.h, rows, self.gu, PRO_RMSNORM, lw["ffn_norm"])
             if self.world == 1:
-                self._gemv(lw["down"], self.gu, rows, self.h, PRO_SWIGLU, accumulate=True)
+                self._proj(lw["down"], self.gu, rows, self.h, PRO_SWIGLU, accumulate=True)
             else:
-                self._gemv(lw["down"], self.gu, rows, self.part, PRO_SWIGLU)
+                self._proj(lw["down"], self.gu, rows, self.part, PRO_SWIGLU)
                 self._allreduce_add(rows)
 
     def _head(self, lq: int):
         """Final RMSNorm + output projection of each sequence's last row, then argmax."""
         D = self.cfg.hidden_size
         ow = self.w.output
+        if self.B >= self.GEMM_DECODE_ROWS and ow.qtype.name != "Q4_K" and gemm_supported(ow.qtype, ow.shape[1]):
+            last = self.h[:self.B * lq].view(self.B, lq, D)[:, lq - 1]     # each sequence's last row
+            self._gemm(ow, last, self.B, self.logits, PRO_RMSNORM, self.w.norm, ws=self.dec_gemm_ws)
+            check(lib.xm_argmax(self.logits.data_ptr(), self.B, self.cfg.vocab_size, self.next_ids.data_ptr(),
+                                self._stream()), "argmax")
+            return
         for b0 in range(0, self.B, 8):
             m = min(8, self.B - b0)
             xp = self.h.data_ptr() + ((b0 * lq + lq - 1) * D) * 4
@@ -376,20 +390,36 @@ class LlamaDecoder:
     PREFILL_CHUNK = 64
 
     def _gemm(self, wt: GGUFTensor, x: torch.Tensor, rows: int, y: torch.Tensor, prologue=PRO_NONE, norm=None,
-              accumulate=False):
+              accumulate=False, ws=None):
         """y[:rows] (+)= pro(x[:rows]) @ W.T on the tensor-core GEMM (GEMV groups where the type's row
-        pitch does not suit the GEMM)."""
+        pitch does not suit the GEMM).  `ws`: a fixed workspace (decode steps), else the prefill's."""
         n, k = wt.shape
         if not gemm_supported(wt.qtype, k):
             self._gemv(wt, x, rows, y, prologue, norm, accumulate)
             return
-        need = lib.xm_qgemm_workspace_size_n(rows, n, k)
-        if self._gemm_ws is None or self._gemm_ws.numel() < need:
-            self._gemm_ws = torch.empty(need, dtype=torch.uint8, device=self.dev)
+        if ws is None:
+            need = lib.xm_qgemm_workspace_size_n(rows, n, k)
+            if self._gemm_ws is None or self._gemm_ws.numel() < need:
+                self._gemm_ws = torch.empty(need, dtype=torch.uint8, device=self.dev)
+            ws = self._gemm_ws
         check(lib.xm_qgemm_ex(wt.qtype.type_id, wt.data.data_ptr(), wt.nbytes, n, k, x.data_ptr(), DT_F32, rows,
                               x.stride(0), prologue, norm.data_ptr() if norm is not None else None,
                               self.cfg.norm_eps, None, y.data_ptr(), 1 if accumulate else 0,
-                              self._gemm_ws.data_ptr(), self._gemm_ws.numel(), self._stream()), "qgemm_ex")
+                              ws.data_ptr(), ws.numel(), self._stream()), "qgemm_ex")
+
+    # Decode steps with this many rows or more run the block types whose multi-row GEMV is the
+    # integer-dot kernel (every type but Q4_K, which has the tensor-core GEMV) on the tcgen05 GEMM
+    # instead: at 4-8 rows the dp4a work per weight grows with the rows, while the GEMM's cost per
+    # weight tile is the decode of the tile (Q6_K 4096x14336 at 8 rows: ~40 us against ~100 us).
+    GEMM_DECODE_ROWS = 4
+
+    def _proj(self, wt: GGUFTensor, x: torch.Tensor, rows: int, y: torch.Tensor, prologue=PRO_NONE, norm=None,
+              accumulate=False):
+        """A decode projection: the GEMV, or the GEMM for 4+ rows of a non-Q4_K weight."""
+        if rows >= self.GEMM_DECODE_ROWS and wt.qtype.name != "Q4_K" and gemm_supported(wt.qtype, wt.shape[1]):
+            self._gemm(wt, x, rows, y, prologue, norm, accumulate, ws=self.dec_gemm_ws)
+        else:
+            self._gemv(wt, x, rows, y, prologue, norm, accumulate)
 
     def _prefill_gemm(self, ids: torch.Tensor) -> torch.Tensor:
         cfg, B = self.cfg, self.B
