@@ -167,22 +167,24 @@ template <> XM_DEV void ld4f<__half>(const __half* p, float (&v)[4]) {
 }
 
 // block-wide max / sum of one value per thread (kPrepThreads threads; red: 32 floats)
+template <int NTH = kPrepThreads>
 XM_DEV float block_max(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
   float r = red[0];
-  for (int w = 1; w < kPrepThreads / 32; ++w) r = fmaxf(r, red[w]);
+  for (int w = 1; w < NTH / 32; ++w) r = fmaxf(r, red[w]);
   __syncthreads();
   return r;
 }
+template <int NTH = kPrepThreads>
 XM_DEV float block_sum(float v, float* red) {
   v = warp_sum(v);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
   float r = red[0];
-  for (int w = 1; w < kPrepThreads / 32; ++w) r += red[w];
+  for (int w = 1; w < NTH / 32; ++w) r += red[w];
   __syncthreads();
   return r;
 }
@@ -209,19 +211,19 @@ XM_DEV int fp16_row_shift(float amax) {
 }
 
 // One row: val(k, v) writes the 4 values at k (k % 4 == 0); out[k] = fp16(v / 2^s),
-// *scale = 2^s.  Every thread of the block calls it; K % 4 == 0.
-template <typename F>
-XM_DEV void prep_row_fp16(F val, int K, __half* __restrict__ out, float* __restrict__ scale, float* red) {
+// *scale = 2^s.  Every thread of the block (NTH threads) calls it; K % 4 == 0.
+template <int NTH, typename F>
+XM_DEV void prep_row_fp16_n(F val, int K, __half* __restrict__ out, float* __restrict__ scale, float* red) {
   float amax = 0.f;
-  for (int k = threadIdx.x * 4; k < K; k += kPrepThreads * 4) {
+  for (int k = threadIdx.x * 4; k < K; k += NTH * 4) {
     float v[4];
     val(k, v);
     amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3]))));
   }
-  amax = block_max(amax, red);
+  amax = block_max<NTH>(amax, red);
   const int s = fp16_row_shift(amax);
   const float inv = ldexpf(1.0f, -s);
-  for (int k = threadIdx.x * 4; k < K; k += kPrepThreads * 4) {
+  for (int k = threadIdx.x * 4; k < K; k += NTH * 4) {
     float v[4];
     val(k, v);
     const __half2 a = __floats2half2_rn(v[0] * inv, v[1] * inv), b = __floats2half2_rn(v[2] * inv, v[3] * inv);
@@ -229,4 +231,8 @@ XM_DEV void prep_row_fp16(F val, int K, __half* __restrict__ out, float* __restr
                                                     *reinterpret_cast<const uint32_t*>(&b));
   }
   if (threadIdx.x == 0) *scale = ldexpf(1.0f, s);
+}
+template <typename F>
+XM_DEV void prep_row_fp16(F val, int K, __half* __restrict__ out, float* __restrict__ scale, float* red) {
+  prep_row_fp16_n<kPrepThreads>(val, K, out, scale, red);
 }

@@ -136,10 +136,12 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int n) {
 // PRO is an XM_PRO_* prologue, applied in fp32 in the reference's order:
 //   XM_PRO_RMSNORM  v = (x / sqrt(mean(x^2) + eps)) * norm_w   (ops.py:115-117)
 //   XM_PRO_SWIGLU   v = silu(x[:K]) * x[K:2K]                  (forward.py:97-98)
-// `ldx` is the row pitch of x in elements.
+// `ldx` is the row pitch of x in elements.  NTH threads per block: 256, or
+// 1024 when the rows are too few to occupy the device (a decode step's 4-8
+// rows), so that each row's two passes are short.
 // ---------------------------------------------------------------------------
-template <typename XT, int PRO>
-__global__ void __launch_bounds__(kPrepThreads) k_prep_rows(const XT* __restrict__ x, int M, int K, int64_t ldx,
+template <typename XT, int PRO, int NTH = kPrepThreads>
+__global__ void __launch_bounds__(NTH) k_prep_rows(const XT* __restrict__ x, int M, int K, int64_t ldx,
                                                             const float* __restrict__ norm_w, float eps,
                                                             __half* __restrict__ x16, float* __restrict__ rowscale) {
   __shared__ float red[32];
@@ -148,14 +150,14 @@ __global__ void __launch_bounds__(kPrepThreads) k_prep_rows(const XT* __restrict
   float rms = 1.f;
   if constexpr (PRO == XM_PRO_RMSNORM) {
     float ss = 0.f;
-    for (int k = threadIdx.x * 4; k < K; k += kPrepThreads * 4) {
+    for (int k = threadIdx.x * 4; k < K; k += NTH * 4) {
       float v[4];
       ld4f<XT>(xr + k, v);
       ss = fmaf(v[0], v[0], fmaf(v[1], v[1], fmaf(v[2], v[2], fmaf(v[3], v[3], ss))));
     }
-    rms = sqrtf(block_sum(ss, red) / (float)K + eps);
+    rms = sqrtf(block_sum<NTH>(ss, red) / (float)K + eps);
   }
-  prep_row_fp16(
+  prep_row_fp16_n<NTH>(
       [&](int k, float (&v)[4]) {
         ld4f<XT>(xr + k, v);
         if constexpr (PRO == XM_PRO_RMSNORM) {
@@ -2349,20 +2351,25 @@ extern "C" int64_t xm_qgemm_workspace_size_n(int64_t m, int64_t n, int64_t k) {
 }
 
 namespace {
-template <typename XT>
-void launch_prep(const void* x, int prologue, int64_t m, int64_t k, int64_t ldx, const float* norm_w, float eps,
-                 __half* x16, float* rowscale, cudaStream_t st) {
+template <typename XT, int NTH>
+void launch_prep_n(const void* x, int prologue, int64_t m, int64_t k, int64_t ldx, const float* norm_w, float eps,
+                   __half* x16, float* rowscale, cudaStream_t st) {
   const unsigned pgrid = (unsigned)m;        // one block per row
   const XT* xt = (const XT*)x;
   if (prologue == XM_PRO_RMSNORM)
-    k_prep_rows<XT, XM_PRO_RMSNORM><<<pgrid, kPrepThreads, 0, st>>>(xt, (int)m, (int)k, ldx, norm_w, eps, x16,
-                                                                    rowscale);
+    k_prep_rows<XT, XM_PRO_RMSNORM, NTH><<<pgrid, NTH, 0, st>>>(xt, (int)m, (int)k, ldx, norm_w, eps, x16, rowscale);
   else if (prologue == XM_PRO_SWIGLU)
-    k_prep_rows<XT, XM_PRO_SWIGLU><<<pgrid, kPrepThreads, 0, st>>>(xt, (int)m, (int)k, ldx, norm_w, eps, x16,
-                                                                   rowscale);
+    k_prep_rows<XT, XM_PRO_SWIGLU, NTH><<<pgrid, NTH, 0, st>>>(xt, (int)m, (int)k, ldx, norm_w, eps, x16, rowscale);
   else
-    k_prep_rows<XT, XM_PRO_NONE><<<pgrid, kPrepThreads, 0, st>>>(xt, (int)m, (int)k, ldx, norm_w, eps, x16,
-                                                                 rowscale);
+    k_prep_rows<XT, XM_PRO_NONE, NTH><<<pgrid, NTH, 0, st>>>(xt, (int)m, (int)k, ldx, norm_w, eps, x16, rowscale);
+}
+template <typename XT>
+void launch_prep(const void* x, int prologue, int64_t m, int64_t k, int64_t ldx, const float* norm_w, float eps,
+                 __half* x16, float* rowscale, cudaStream_t st) {
+  if (m < 2 * sm_count_dev())
+    launch_prep_n<XT, 1024>(x, prologue, m, k, ldx, norm_w, eps, x16, rowscale, st);
+  else
+    launch_prep_n<XT, kPrepThreads>(x, prologue, m, k, ldx, norm_w, eps, x16, rowscale, st);
 }
 }  // namespace
 
