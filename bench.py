@@ -620,7 +620,7 @@ def decode_section(args, rank, world, dev, peaks):
                    "projection_TFLOPS": round(pf_tf, 1),
                    "frac_of_measured_bf16_peak": round(pf_tf / float(peaks.get("bf16_tflops", 1590.0)), 4),
                    "path": "every projection over all B*512 rows on the tcgen05 GEMM (fused RMSNorm / SwiGLU / "
-                           "residual), attention in 64-token chunks, output head on the last token"}
+                           "residual), causal GQA attention of the whole prompt on tensor cores (one call per layer), split-K where the output tiles are few, output head on the last token"}
         dec.decode_step()
         dec.length += 1
         dec.capture()
