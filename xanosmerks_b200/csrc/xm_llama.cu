@@ -277,11 +277,24 @@ __global__ void __launch_bounds__(256) k_attention(const float* __restrict__ qkv
 // running max and sum per row, P (fp16) reuses the S fragments as the A
 // operand of P V (ldmatrix.trans of the V rows), and O / l is written as fp32.
 // Keys past the last written position read as zeros in shared memory and are
-// masked, so no uninitialised cache entry enters a product.
+// masked, so no uninitialised cache entry enters a product.  The K / V tiles
+// are double-buffered (dynamic shared memory, 2 x 2 x 64 x 272 bytes): the
+// next tile's 16-byte cp.async copies are in flight while the warps compute
+// on the current one.
 // ---------------------------------------------------------------------------
 constexpr int kChunkTok = 16;           // new tokens per CTA (the MMA's M)
 constexpr int kKeyTile = 64;
 constexpr int kRowH = kHeadDim + 8;     // halves per staged row (272 bytes)
+constexpr int kAttnTileHalves = kKeyTile * kRowH;                      // one staged K or V tile
+constexpr int kAttnSmem = 2 * 2 * kAttnTileHalves * (int)sizeof(__half);   // 2 buffers of K and V: 69,632 bytes
+
+// 16-byte global -> shared copy; src_bytes = 0 writes zeros and reads nothing
+XM_DEV void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+XM_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+XM_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 __global__ void __launch_bounds__(128) k_kv_append(const float* __restrict__ qkv, int64_t qkv_stride,
                                                    __half* __restrict__ kc, __half* __restrict__ vc,
@@ -330,8 +343,7 @@ __global__ void __launch_bounds__(32 * kMaxGroup) k_attn_chunk(const float* __re
                                                                const int* __restrict__ pos0, int Lq, int Hq, int Hk,
                                                                int max_ctx, float theta, float* __restrict__ out,
                                                                int64_t out_stride) {
-  __shared__ __align__(16) __half ks[kKeyTile][kRowH];
-  __shared__ __align__(16) __half vs[kKeyTile][kRowH];
+  extern __shared__ __align__(16) __half attn_sm[];   // [buffer][K, V][key][kRowH]
   grid_dep_wait();                                 // the appended keys come from the preceding kernel
   grid_dep_launch();
   const int b = blockIdx.x / Hk, hk = blockIdx.x % Hk;
@@ -379,24 +391,36 @@ __global__ void __launch_bounds__(32 * kMaxGroup) k_attn_chunk(const float* __re
 #pragma unroll
   for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
   float ma = -INFINITY, mb = -INFINITY, la = 0.f, lb = 0.f;
-  const uint32_t ks0 = (uint32_t)__cvta_generic_to_shared(&ks[0][0]);
-  const uint32_t vs0 = (uint32_t)__cvta_generic_to_shared(&vs[0][0]);
+  const uint32_t sm0 = (uint32_t)__cvta_generic_to_shared(attn_sm);
   const int mi = lane >> 3, mr = lane & 7;        // ldmatrix: this lane addresses row mr of matrix mi
-
-  for (int kb = 0; kb < kend; kb += kKeyTile) {
-    __syncthreads();                               // the previous tile is no longer read
+  // tile kb -> buffer buf (K at buffer offset 0, V after it); keys >= kend are zero-filled
+  auto stage = [&](int kb, int buf) {
+    const uint32_t kdst = sm0 + (uint32_t)(buf * 2 * kAttnTileHalves) * 2u;
+    const uint32_t vdst = kdst + (uint32_t)kAttnTileHalves * 2u;
     for (int i = tid; i < kKeyTile * (kHeadDim / 8); i += nthr) {
       const int r = i / (kHeadDim / 8), c = (i % (kHeadDim / 8)) * 8;
       const int key = kb + r;
-      uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-      if (key < kend) {
-        kv = *reinterpret_cast<const uint4*>(K + (int64_t)key * kHeadDim + c);
-        vv = *reinterpret_cast<const uint4*>(V + (int64_t)key * kHeadDim + c);
-      }
-      *reinterpret_cast<uint4*>(&ks[r][c]) = kv;
-      *reinterpret_cast<uint4*>(&vs[r][c]) = vv;
+      const bool ok = key < kend;
+      const int64_t off = (int64_t)(ok ? key : 0) * kHeadDim + c;
+      const uint32_t so = (uint32_t)(r * kRowH + c) * 2u;
+      cp_async16(kdst + so, K + off, ok ? 16u : 0u);
+      cp_async16(vdst + so, V + off, ok ? 16u : 0u);
     }
-    __syncthreads();
+    cp_async_commit();
+  };
+  stage(0, 0);
+
+  for (int kb = 0, t = 0; kb < kend; kb += kKeyTile, ++t) {
+    __syncthreads();                               // every warp is done with the tile read two steps ago
+    if (kb + kKeyTile < kend) {
+      stage(kb + kKeyTile, (t + 1) & 1);           // the next tile loads while this one is used
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();                               // this tile's copies of every thread have landed
+    const uint32_t ks0 = sm0 + (uint32_t)((t & 1) * 2 * kAttnTileHalves) * 2u;
+    const uint32_t vs0 = ks0 + (uint32_t)kAttnTileHalves * 2u;
     // S = q k^T: 8 tiles of 8 keys
     float sc[8][4];
 #pragma unroll
@@ -530,10 +554,12 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ logit
 }
 
 template <typename... KArgs, typename... Args>
-cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+cudaError_t launch_pdl_smem(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, int smem,
+                            Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
+  cfg.dynamicSmemBytes = (size_t)smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -541,6 +567,10 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStre
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+  return launch_pdl_smem(kernel, grid, block, st, 0, args...);
 }
 
 int launch_status(cudaError_t e, const char* what) {
@@ -599,8 +629,16 @@ int xm_attention(const float* d_qkv, int64_t qkv_stride, void* d_kcache, void* d
                                       (int)max_ctx, theta),
                            "attention kv append");
     if (rc) return rc;
-    return launch_status(launch_pdl(k_attn_chunk, dim3((unsigned)(B * Hk), (unsigned)((Lq + kChunkTok - 1) / kChunkTok)),
-                                    dim3((unsigned)(32 * G)), (cudaStream_t)stream, d_qkv, qkv_stride,
+    static bool attn_attr[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attn_attr[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(k_attn_chunk, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
+      if (e != cudaSuccess) return xm_set_error(XM_ERR_CUDA, "attention: smem attribute: %s", cudaGetErrorString(e));
+      if (dev >= 0 && dev < 64) attn_attr[dev] = true;
+    }
+    return launch_status(launch_pdl_smem(k_attn_chunk, dim3((unsigned)(B * Hk), (unsigned)((Lq + kChunkTok - 1) / kChunkTok)),
+                                    dim3((unsigned)(32 * G)), (cudaStream_t)stream, kAttnSmem, d_qkv, qkv_stride,
                                     (const __half*)d_kcache, (const __half*)d_vcache, d_pos0, Lq, Hq, Hk,
                                     (int)max_ctx, theta, d_out, out_stride),
                          "attention chunk");
