@@ -197,6 +197,21 @@ int xm_qgemm_ex(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t 
                 void* d_workspace, int64_t workspace_bytes, void* stream);
 
 /*
+ * xm_qgemm_ex on weight rows stored `w_row_pitch` bytes apart (a multiple of
+ * 16, at least the row's record bytes; w_bytes >= (n - 1) * pitch + row
+ * bytes).  For K-slices whose rows are not whole 16-byte units (a Q6_K slice
+ * of 7168 columns is 5880 bytes per row): the caller keeps a copy of the slice
+ * with each row padded to the pitch, and the tensor-core GEMM reads that copy.
+ * The padding bytes are never decoded.  Same replacement as xm_qgemm_ex, for
+ * the row-parallel projections of a tensor-parallel model (the K-sliced
+ * `x @ W.T` of forward.py:97-101 on one rank).
+ */
+int xm_qgemm_ex_pitched(int qtype, const void* d_w, int64_t w_row_pitch, int64_t w_bytes, int64_t n,
+                        int64_t k, const void* d_x, int x_dtype, int64_t m, int64_t x_stride, int prologue,
+                        const float* d_norm_w, float eps, const float* d_bias, float* d_y, int accumulate,
+                        void* d_workspace, int64_t workspace_bytes, void* stream);
+
+/*
  * RMSNorm of m rows of x (row pitch x_stride elements): out[m][k] fp32 =
  * (x / sqrt(mean(x^2) + eps)) * norm_w, in the reference's order
  * (primitives.py:20-23, ops.py:115-117).  The norm of FusedRMSNormLinearOp

@@ -209,3 +209,34 @@ def test_gemm_split_k(name, m, n, k, accumulate):
     tol = 1e-5 * max(1.0, k / 4096)
     assert rel_err(ys[0].cpu().numpy(), ref) < tol, rel_err(ys[0].cpu().numpy(), ref)
     assert rel_err(ys[0].cpu().numpy(), y1.cpu().numpy()) < tol
+
+
+@pytest.mark.parametrize("m,n,k,accumulate", [(40, 300, 1792, False), (512, 4096, 7168, True), (96, 512, 3584, False)])
+def test_gemm_pitched_rows(m, n, k, accumulate):
+    """xm_qgemm_ex_pitched: Q6_K K-slices whose rows are not whole 16-byte units (the tensor-parallel down
+    projection's slices: 1792 / 7168 / 3584 columns = 1470 / 5880 / 2940 bytes) padded to a 16-byte pitch."""
+    raw, w = wref("Q6_K", n, k, 131)
+    rb = len(raw) // n
+    assert rb % 16
+    pitch = (rb + 15) // 16 * 16
+    pad = torch.zeros(n, pitch, dtype=torch.uint8)
+    pad[:, :rb] = torch.from_numpy(np.frombuffer(raw, dtype=np.uint8).reshape(n, rb).copy())
+    pad = pad.cuda()
+    rng = np.random.default_rng(132)
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(133)).to(torch.bfloat16)
+    b = torch.from_numpy(rng.standard_normal(n).astype(np.float32)).cuda()
+    h0 = rng.standard_normal((m, n)).astype(np.float32) if accumulate else np.zeros((m, n), np.float32)
+    y = torch.from_numpy(h0.copy()).cuda()
+    xd = x.cuda()
+    ws = torch.empty(_lib.lib.xm_qgemm_workspace_size_n(m, n, k), dtype=torch.uint8, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.check(_lib.lib.xm_qgemm_ex_pitched(14, pad.data_ptr(), pitch, pad.numel(), n, k, xd.data_ptr(),
+                                            _lib.DT_BF16, m, k, _lib.PRO_NONE, None, 1e-5, b.data_ptr(), y.data_ptr(),
+                                            1 if accumulate else 0, ws.data_ptr(), ws.numel(), st), "pitched")
+    torch.cuda.synchronize()
+    ref = h0 + x.float().numpy() @ w.T + b.cpu().numpy()
+    assert rel_err(y.cpu().numpy(), ref) < 1e-5 * max(1.0, k / 4096), rel_err(y.cpu().numpy(), ref)
+    for bad in (rb, pitch - 16, pitch + 8):          # not a multiple of 16, or shorter than a row
+        assert _lib.lib.xm_qgemm_ex_pitched(14, pad.data_ptr(), bad, pad.numel(), n, k, xd.data_ptr(), _lib.DT_BF16,
+                                            m, k, _lib.PRO_NONE, None, 1e-5, None, y.data_ptr(), 0, ws.data_ptr(),
+                                            ws.numel(), st) == _lib.XM_ERR_INVALID

@@ -45,6 +45,8 @@ SIGNATURES = {
     "xm_qgemm": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _int, _i64, _vp, _vp, _vp, _i64, _vp]),
     "xm_qgemm_ex": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _int, _i64, _i64, _int, _vp, _f32, _vp, _vp, _int,
                            _vp, _i64, _vp]),
+    "xm_qgemm_ex_pitched": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _vp, _int, _i64, _i64, _int, _vp, _f32, _vp,
+                                   _vp, _int, _vp, _i64, _vp]),
     "xm_moe_workspace_size": (_i64, [_i64, _i64, _i64, _int, _int]),
     "xm_moe_forward": (_int, [_vp, _int, _i64, _i64, _vp, _int, _int, _i64, ctypes.POINTER(_vp),
                               ctypes.POINTER(_vp), ctypes.POINTER(_vp), _int, _int, _vp, _vp, _i64, _vp]),

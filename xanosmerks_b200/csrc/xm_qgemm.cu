@@ -1809,10 +1809,12 @@ int64_t pair_row_bytes(int64_t k) {
 }
 
 template <int T>
-int encode_w_records(CUtensorMap* map, const uint8_t* w, int64_t n, int64_t k, int rows_per_box) {
+int encode_w_records(CUtensorMap* map, const uint8_t* w, int64_t n, int64_t k, int rows_per_box,
+                     int64_t pitch = 0) {
   EncodeTiledFn encode = get_encode();
   if (!encode) return xm_set_error(XM_ERR_CUDA, "qgemm: cuTensorMapEncodeTiled unavailable");
-  const int64_t row_bytes = pair_row_bytes<T>(k);
+  // rows `pitch` bytes apart (0: packed rows); the bytes past a row's records are never decoded
+  const int64_t row_bytes = pitch ? pitch : pair_row_bytes<T>(k);
   const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 2), (cuuint64_t)n};
   const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
   const cuuint32_t box[2] = {(cuuint32_t)(ColGeom<T>::BB / 2), (cuuint32_t)rows_per_box};
@@ -2111,7 +2113,7 @@ int launch_tm(const CUtensorMap& map_b, const PairW<NMAP>& pw, const PairW<NMAP>
 template <int T>
 int launch_tm_gemm(const __half* a16, const uint8_t* w, int64_t m, int64_t n, int64_t k, const float* rowscale,
                    const float* bias, float* y, int acc, cudaStream_t st, float* part = nullptr,
-                   int64_t part_bytes = 0) {
+                   int64_t part_bytes = 0, int64_t w_pitch = 0) {
   constexpr int BB = ColGeom<T>::BB;
   const void* fn = tm_kernel<T, 1>();
   const TmCfg probe = tm_stages(128, BB);
@@ -2129,7 +2131,7 @@ int launch_tm_gemm(const __half* a16, const uint8_t* w, int64_t m, int64_t n, in
   int rc = encode_a16(&map_b, a16, m, k, cfg.NT / 2);
   if (rc) return rc;
   PairW<1> pw{};
-  rc = encode_w_records<T>(&pw.map[0], w, n, k, kTmRows);
+  rc = encode_w_records<T>(&pw.map[0], w, n, k, kTmRows, w_pitch);
   if (rc) return rc;
   pw.groups = 1;
   const int64_t tm = (m + cfg.NT - 1) / cfg.NT;
@@ -2222,11 +2224,13 @@ struct PairDense {
   const __half* a16;
   float* part;                     // split-K partial planes (workspace beyond the activation), or null
   int64_t part_bytes;
+  int64_t w_pitch;                 // weight row pitch in bytes (0: packed rows)
   int rc = 1;
   template <int T>
   void operator()() {
-    // tensor-memory-A kernel; the CTA-pair kernel where the device cannot hold it
-    rc = launch_tm_gemm<T>(a16, w, m, n, k, rowscale, bias, y, acc, st, part, part_bytes);
+    // tensor-memory-A kernel; the CTA-pair kernel where the device cannot hold it (packed rows only)
+    rc = launch_tm_gemm<T>(a16, w, m, n, k, rowscale, bias, y, acc, st, part, part_bytes, w_pitch);
+    if (rc == 1 && w_pitch) rc = xm_set_error(XM_ERR_UNSUPPORTED, "qgemm: pitched weights need the CTA-pair kernel");
     if (rc == 1) rc = launch_pair_gemm<T>(*map_a, w, m, n, k, rowscale, bias, y, acc, st);
   }
 };
@@ -2373,10 +2377,11 @@ void launch_prep(const void* x, int prologue, int64_t m, int64_t k, int64_t ldx,
 }
 }  // namespace
 
-extern "C" int xm_qgemm_ex(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k, const void* d_x,
-                           int x_dtype, int64_t m, int64_t x_stride, int prologue, const float* d_norm_w, float eps,
-                           const float* d_bias, float* d_y, int accumulate, void* d_workspace,
-                           int64_t workspace_bytes, void* stream) {
+namespace {
+int qgemm_ex_impl(int qtype, const void* d_w, int64_t w_pitch, int64_t w_bytes, int64_t n, int64_t k, const void* d_x,
+                  int x_dtype, int64_t m, int64_t x_stride, int prologue, const float* d_norm_w, float eps,
+                  const float* d_bias, float* d_y, int accumulate, void* d_workspace, int64_t workspace_bytes,
+                  void* stream) {
   int qk = 0, rec = 0;
   if (!host_qtype_geometry(qtype, &qk, &rec) || qk == 1)
     return xm_set_error(XM_ERR_UNSUPPORTED, "qgemm: type id %d is not a block-quantized type", qtype);
@@ -2391,13 +2396,17 @@ extern "C" int xm_qgemm_ex(int qtype, const void* d_w, int64_t w_bytes, int64_t 
   if (x_stride < (prologue == XM_PRO_SWIGLU ? 2 * k : k))
     return xm_set_error(XM_ERR_INVALID, "qgemm: x_stride %lld too small", (long long)x_stride);
   const int64_t row_bytes = qgemm_row_bytes(qtype, k);
-  if (n * row_bytes > w_bytes)
-    return xm_set_error(XM_ERR_INVALID, "qgemm: weight needs %lld bytes, got %lld", (long long)(n * row_bytes),
+  if (w_pitch && (w_pitch < row_bytes || w_pitch % 16))
+    return xm_set_error(XM_ERR_INVALID, "qgemm: row pitch %lld must be a multiple of 16 and at least the row's %lld "
+                        "bytes", (long long)w_pitch, (long long)row_bytes);
+  const int64_t need_w = w_pitch ? (n - 1) * w_pitch + row_bytes : n * row_bytes;
+  if (need_w > w_bytes)
+    return xm_set_error(XM_ERR_INVALID, "qgemm: weight needs %lld bytes, got %lld", (long long)need_w,
                         (long long)w_bytes);
-  if (row_bytes % 16)
+  if (!w_pitch && row_bytes % 16)
     return xm_set_error(XM_ERR_UNSUPPORTED,
                         "qgemm: a row of type id %d with k=%lld is %lld bytes, not a multiple of 16 (tensor-map "
-                        "pitch); use the GEMV on row groups",
+                        "pitch); use the GEMV on row groups, or rows padded to a 16-byte pitch",
                         qtype, (long long)k, (long long)row_bytes);
   if (!d_w || !d_x || !d_y || !d_workspace) return xm_set_error(XM_ERR_INVALID, "qgemm: null pointer");
   if (((uintptr_t)d_w & 15) || ((uintptr_t)d_workspace & 255) || ((uintptr_t)d_x & 15))
@@ -2427,15 +2436,34 @@ extern "C" int xm_qgemm_ex(int qtype, const void* d_w, int64_t w_bytes, int64_t 
     part_bytes = workspace_bytes - qgemm_part_offset(m, k);
   }
   PairDense pd{&map_a, (const uint8_t*)d_w, m, n, k, rowscale, d_bias, d_y, accumulate ? 1 : 0, st, x16, part,
-               part_bytes};
+               part_bytes, w_pitch};
   dispatch_quant(qtype, pd);
   if (pd.rc != 1) return pd.rc;
   if (qtype != T_Q4_K)
     return xm_set_error(XM_ERR_UNSUPPORTED, "qgemm: this device cannot hold the CTA-pair kernel");
+  if (w_pitch) return xm_set_error(XM_ERR_UNSUPPORTED, "qgemm: pitched weights need the CTA-pair kernel");
   const TileCfg cfg = choose_tile(m, n, k, sm_count_dev());
   const dim3 grid((unsigned)((n + cfg.BN - 1) / cfg.BN), (unsigned)((m + cfg.MT * 128 - 1) / (cfg.MT * 128)));
   return launch_gemm(map_a, (const uint8_t*)d_w, m, n, k, cfg, grid, rowscale, d_bias, d_y, accumulate ? 1 : 0,
                      GemmGroups{}, st);
+}
+}  // namespace
+
+extern "C" int xm_qgemm_ex(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k, const void* d_x,
+                           int x_dtype, int64_t m, int64_t x_stride, int prologue, const float* d_norm_w, float eps,
+                           const float* d_bias, float* d_y, int accumulate, void* d_workspace,
+                           int64_t workspace_bytes, void* stream) {
+  return qgemm_ex_impl(qtype, d_w, 0, w_bytes, n, k, d_x, x_dtype, m, x_stride, prologue, d_norm_w, eps, d_bias, d_y,
+                       accumulate, d_workspace, workspace_bytes, stream);
+}
+
+extern "C" int xm_qgemm_ex_pitched(int qtype, const void* d_w, int64_t w_row_pitch, int64_t w_bytes, int64_t n,
+                                   int64_t k, const void* d_x, int x_dtype, int64_t m, int64_t x_stride, int prologue,
+                                   const float* d_norm_w, float eps, const float* d_bias, float* d_y, int accumulate,
+                                   void* d_workspace, int64_t workspace_bytes, void* stream) {
+  if (w_row_pitch <= 0) return xm_set_error(XM_ERR_INVALID, "qgemm: row pitch must be positive");
+  return qgemm_ex_impl(qtype, d_w, w_row_pitch, w_bytes, n, k, d_x, x_dtype, m, x_stride, prologue, d_norm_w, eps,
+                       d_bias, d_y, accumulate, d_workspace, workspace_bytes, stream);
 }
 
 extern "C" int xm_qgemm(int qtype, const void* d_w, int64_t w_bytes, int64_t n, int64_t k, const void* d_x,

@@ -232,6 +232,22 @@ class LlamaDecoder:
                 r = self.B if wt is self.w.output else rows
                 dec_need = max(dec_need, lib.xm_qgemm_workspace_size_n(r, wt.shape[0], wt.shape[1]))
         self.dec_gemm_ws = torch.zeros(dec_need, dtype=torch.uint8, device=dev)
+        # K-slices whose rows are not whole 16-byte units (tensor-parallel Q6_K down projections: 7168
+        # columns are 5880 bytes a row) keep a copy with each row padded to a 16-byte pitch for the
+        # GEMM (prefill and 4+-row steps); the GEMV reads the packed slice
+        self._pitched = {}
+        for lw in self.w.layers:
+            for wt in lw.values():
+                if not (isinstance(wt, GGUFTensor) and len(wt.shape) == 2):
+                    continue
+                n, k = wt.shape
+                rb = qtypes.row_bytes(wt.qtype, k)
+                if k % 256 or rb % 16 == 0:
+                    continue
+                pitch = (rb + 15) // 16 * 16
+                pad = torch.zeros(n, pitch, dtype=torch.uint8, device=dev)
+                pad[:, :rb] = wt.data.view(n, rb)
+                self._pitched[wt.data.data_ptr()] = (pad, pitch)
         if collective not in ("p2p", "nccl"):
             raise ValueError(f"collective must be 'p2p' or 'nccl', got {collective!r}")
         self.collective = collective
@@ -394,7 +410,8 @@ class LlamaDecoder:
         """y[:rows] (+)= pro(x[:rows]) @ W.T on the tensor-core GEMM (GEMV groups where the type's row
         pitch does not suit the GEMM).  `ws`: a fixed workspace (decode steps), else the prefill's."""
         n, k = wt.shape
-        if not gemm_supported(wt.qtype, k):
+        pitched = self._pitched.get(wt.data.data_ptr())
+        if not gemm_supported(wt.qtype, k) and pitched is None:
             self._gemv(wt, x, rows, y, prologue, norm, accumulate)
             return
         if ws is None:
@@ -402,10 +419,17 @@ class LlamaDecoder:
             if self._gemm_ws is None or self._gemm_ws.numel() < need:
                 self._gemm_ws = torch.empty(need, dtype=torch.uint8, device=self.dev)
             ws = self._gemm_ws
+        norm_p = norm.data_ptr() if norm is not None else None
+        if pitched is not None:
+            pad, pitch = pitched
+            check(lib.xm_qgemm_ex_pitched(wt.qtype.type_id, pad.data_ptr(), pitch, pad.numel(), n, k, x.data_ptr(),
+                                          DT_F32, rows, x.stride(0), prologue, norm_p, self.cfg.norm_eps, None,
+                                          y.data_ptr(), 1 if accumulate else 0, ws.data_ptr(), ws.numel(),
+                                          self._stream()), "qgemm_ex_pitched")
+            return
         check(lib.xm_qgemm_ex(wt.qtype.type_id, wt.data.data_ptr(), wt.nbytes, n, k, x.data_ptr(), DT_F32, rows,
-                              x.stride(0), prologue, norm.data_ptr() if norm is not None else None,
-                              self.cfg.norm_eps, None, y.data_ptr(), 1 if accumulate else 0,
-                              ws.data_ptr(), ws.numel(), self._stream()), "qgemm_ex")
+                              x.stride(0), prologue, norm_p, self.cfg.norm_eps, None, y.data_ptr(),
+                              1 if accumulate else 0, ws.data_ptr(), ws.numel(), self._stream()), "qgemm_ex")
 
     # Decode steps with this many rows or more run the block types whose multi-row GEMV is the
     # integer-dot kernel (every type but Q4_K, which has the tensor-core GEMV) on the tcgen05 GEMM
@@ -416,7 +440,8 @@ class LlamaDecoder:
     def _proj(self, wt: GGUFTensor, x: torch.Tensor, rows: int, y: torch.Tensor, prologue=PRO_NONE, norm=None,
               accumulate=False):
         """A decode projection: the GEMV, or the GEMM for 4+ rows of a non-Q4_K weight."""
-        if rows >= self.GEMM_DECODE_ROWS and wt.qtype.name != "Q4_K" and gemm_supported(wt.qtype, wt.shape[1]):
+        if rows >= self.GEMM_DECODE_ROWS and wt.qtype.name != "Q4_K" and (
+                gemm_supported(wt.qtype, wt.shape[1]) or wt.data.data_ptr() in self._pitched):
             self._gemm(wt, x, rows, y, prologue, norm, accumulate, ws=self.dec_gemm_ws)
         else:
             self._gemv(wt, x, rows, y, prologue, norm, accumulate)
